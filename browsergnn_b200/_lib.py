@@ -1,0 +1,134 @@
+"""ctypes binding of libbgnn_cuda.so (include/bgnn.h).
+
+The library is the only compute path: if it is missing or no CUDA device is
+present, every operation raises -- there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "libbgnn_cuda.so")
+
+# bgnn_status
+OK, ERR_INVALID_ARG, ERR_OUT_OF_RANGE, ERR_CUDA, ERR_NO_MEMORY, ERR_TIMEOUT, ERR_UNSUPPORTED, \
+    ERR_DEVICE = range(8)
+MATH_FAST, MATH_EXACT = 0, 1
+AGGR = {"sum": 0, "add": 0, "mean": 1, "max": 2}
+ACT = {None: 0, "none": 0, "relu": 1, "relu_max": 2, "elu": 3, "leaky_relu": 4}
+
+STATUS_NAMES = {
+    OK: "OK", ERR_INVALID_ARG: "INVALID_ARG", ERR_OUT_OF_RANGE: "OUT_OF_RANGE", ERR_CUDA: "CUDA",
+    ERR_NO_MEMORY: "NO_MEMORY", ERR_TIMEOUT: "TIMEOUT", ERR_UNSUPPORTED: "UNSUPPORTED",
+    ERR_DEVICE: "DEVICE",
+}
+
+
+class BGNNError(RuntimeError):
+    """A non-OK status returned by libbgnn_cuda."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(f"[{STATUS_NAMES.get(status, status)}] {message}")
+        self.status = status
+
+
+class BGNNIndexError(BGNNError, ValueError):
+    """An index out of range (the reference throws an Error from GraphData)."""
+
+
+_P = ctypes.c_void_p
+_U32 = ctypes.c_uint32
+_U64 = ctypes.c_uint64
+_I = ctypes.c_int
+_D = ctypes.c_double
+_F = ctypes.c_float
+
+# name -> argtypes (all return int unless listed in _RESTYPE)
+SIGNATURES = {
+    "bgnn_abi_version": [],
+    "bgnn_ctx_create": [_I, ctypes.POINTER(_P)],
+    "bgnn_ctx_destroy": [_P],
+    "bgnn_ctx_set_stream": [_P, _P],
+    "bgnn_ctx_set_math": [_P, _I],
+    "bgnn_ctx_synchronize": [_P],
+    "bgnn_last_error": [_P],
+    "bgnn_ctx_launch_count": [_P],
+    "bgnn_spmm_host": [_P, _P, _P, _P, _P, _U32, _U32, _U32, _P],
+    "bgnn_scatter_add_host": [_P, _P, _P, _U64, _U32, _U32, _P],
+    "bgnn_scatter_mean_host": [_P, _P, _P, _U64, _U32, _U32, _P],
+    "bgnn_scatter_max_host": [_P, _P, _P, _U64, _U32, _U32, _P],
+    "bgnn_gather_host": [_P, _P, _U32, _P, _U64, _U32, _P],
+    "bgnn_matmul_host": [_P, _P, _P, _U32, _U32, _U32, _P],
+    "bgnn_relu_host": [_P, _P, _U64, _P],
+    "bgnn_add_host": [_P, _P, _P, _U64, _P],
+    "bgnn_spmv_host": [_P, _P, _P, _P, _P, _U32, _U32, _P],
+    "bgnn_spmm_dev": [_P, _P, _P, _P, _P, _U32, _U32, _U32, _P],
+    "bgnn_scatter_dev": [_P, _I, _P, _P, _U64, _U32, _U32, _P],
+    "bgnn_gather_dev": [_P, _P, _U32, _P, _U64, _U32, _P],
+    "bgnn_matmul_dev": [_P, _P, _P, _U32, _U32, _U32, _P],
+    "bgnn_activation_dev": [_P, _I, _D, _P, _U64, _P],
+    "bgnn_add_dev": [_P, _P, _P, _U64, _P],
+    "bgnn_spmv_dev": [_P, _P, _P, _P, _P, _U32, _U32, _P],
+    "bgnn_coo_to_csr_dev": [_P, _P, _P, _P, _U64, _U32, _U32, _P, _P, _P],
+    "bgnn_coo_to_csr_host": [_P, _P, _P, _P, _U64, _U32, _U32, _P, _P, _P],
+    "bgnn_gcn_norm_dev": [_P, _P, _U64, _U32, _I, _P],
+    "bgnn_graph_create": [_P, _P, _U64, _U32, _U32, _I, ctypes.POINTER(_P)],
+    "bgnn_graph_create_csr": [_P, _P, _P, _U32, _U32, ctypes.POINTER(_P)],
+    "bgnn_graph_destroy": [_P],
+    "bgnn_graph_info": [_P, ctypes.POINTER(_U32), ctypes.POINTER(_U32), ctypes.POINTER(_U64),
+                        ctypes.POINTER(_I)],
+    "bgnn_graph_degrees": [_P, _P, _P, _P],
+    "bgnn_graph_csr": [_P, _P, _P, _P, _P],
+    "bgnn_aggregate": [_P, _P, _I, _P, _U32, _P],
+    "bgnn_gcn_propagate": [_P, _P, _P, _U32, _I, _I, _P, _I, _D, _P],
+    "bgnn_gat": [_P, _P, _P, _U32, _U32, _P, _P, _D, _I, _I, _P, _I, _D, _P],
+    "bgnn_gin_aggregate": [_P, _P, _P, _U32, _F, _P],
+    "bgnn_graph_spmm": [_P, _P, _P, _P, _U32, _P],
+    "bgnn_linear": [_P, _P, _P, _U32, _U32, _U32, _P, _I, _D, _P],
+    "bgnn_sage_linear": [_P, _P, _P, _P, _P, _U32, _U32, _U32, _P, _I, _D, _P],
+    "bgnn_l2_normalize_rows": [_P, _P, _U32, _U32],
+    "bgnn_sum_pool": [_P, _P, _U32, _U32, _P, _U32, _P],
+    "bgnn_pack_rows": [_P, _P, _U32, _P, _U32, _U32, _P],
+    "bgnn_pool_projection": [_P, _P, _P, _P, _U32, _U32, _P],
+    "bgnn_synth_rmat": [_P, _U64, _I, _U32, _U64, _D, _D, _D, _I, _P],
+}
+_RESTYPE = {"bgnn_last_error": ctypes.c_char_p, "bgnn_ctx_launch_count": ctypes.c_uint64}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load():
+    """Load libbgnn_cuda.so (raises if it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise RuntimeError(
+                    f"{LIB_PATH} is missing: build it with `python -m browsergnn_b200.build` "
+                    "(there is no CPU fallback)")
+            lib = ctypes.CDLL(LIB_PATH)
+            for name, args in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.argtypes = args
+                fn.restype = _RESTYPE.get(name, ctypes.c_int)
+            if lib.bgnn_abi_version() != 1:
+                raise RuntimeError("libbgnn_cuda ABI version mismatch")
+            _lib = lib
+    return _lib
+
+
+def check(status: int, ctx=None):
+    if status == OK:
+        return
+    msg = ""
+    if ctx is not None:
+        raw = load().bgnn_last_error(ctx)
+        msg = raw.decode() if raw else ""
+    if status == ERR_OUT_OF_RANGE:
+        raise BGNNIndexError(status, msg)
+    raise BGNNError(status, msg)

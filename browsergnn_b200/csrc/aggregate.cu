@@ -1,0 +1,344 @@
+// Fused gather + aggregate over a destination-keyed CSR: sum / mean / max,
+// GCN-normalised sum, and SpMM with per-edge values.  No [E, F] message
+// tensor is ever materialised (the reference builds one per layer with
+// MessagePassing.gather, src/core/sparse.ts:462-473).
+//
+// Bit-exactness: each output element is accumulated by ONE thread, visiting
+// the row's edges in CSR order, which for a graph CSR is the COO edge order
+// the reference's scatters use (src/backend/wasm/index.ts:80-102).  Each step
+// rounds exactly where the reference stores into a Float32Array:
+//   sum   f32(acc + x)                       == __fadd_rn
+//   gcn   f32(acc + f32(x * f32(ds * dd)))   == __fadd_rn(acc, __fmul_rn(x, w))
+//   spmm  f32(acc + v*x) in double           == f64 fma then one rounding
+//   max   x > acc ? x : acc, -inf -> 0 after (index.ts:158-206)
+//   mean  f32(sum * (1/count as double))     (index.ts:128-148)
+// No float atomics, no tree reductions, no FMA contraction (-fmad=false and
+// explicit _rn intrinsics).
+//
+// Two schedules:
+//   light rows  (degree < threshold): a group of G lanes per row, lanes over
+//               features (float4 when the row stride allows), U edges of
+//               row data in flight per lane.
+//   heavy rows  (degree >= threshold): one CTA per (row, 32-feature slice);
+//               256 threads stream the row's source slices into a 4-stage
+//               cp.async shared-memory ring while one warp accumulates them in
+//               edge order.  Heavy rows are sorted by degree (largest first)
+//               and run on a second stream concurrently with the light rows.
+#include "bgnn_internal.cuh"
+
+namespace {
+
+constexpr unsigned FULL = 0xffffffffu;
+constexpr int OP_SPMM_X = 4;  // SpMM with f64 emulation of each JS step
+
+template <int OP>
+__device__ __forceinline__ float step(float acc, float x, float w) {
+  if constexpr (OP == OP_SUM) {
+    return __fadd_rn(acc, x);
+  } else if constexpr (OP == OP_MAX) {
+    return x > acc ? x : acc;
+  } else if constexpr (OP == OP_GCN) {
+    return __fadd_rn(acc, __fmul_rn(x, w));
+  } else if constexpr (OP == OP_SPMM) {
+    return __fmaf_rn(w, x, acc);
+  } else {
+    // the JS product of two f32 values is exact in double; fma rounds the sum once
+    return __double2float_rn(__fma_rn((double)w, (double)x, (double)acc));
+  }
+}
+
+template <int OP>
+__device__ __forceinline__ float init_acc() {
+  return OP == OP_MAX ? -INFINITY : 0.0f;
+}
+
+__device__ __forceinline__ float epilogue(float v, const AggArgs& a, uint32_t row, int f,
+                                          uint32_t cnt) {
+  if (a.mean && cnt > 0) v = __double2float_rn(__dmul_rn((double)v, __ddiv_rn(1.0, (double)cnt)));
+  if (a.max_fix && v == -INFINITY) v = 0.0f;
+  if (a.gin_x) {
+    // GINConv: combined = (1 + eps) * x + aggregated, in double (gin.ts:150-157)
+    const double xs = (double)a.gin_x[(int64_t)row * a.ld_gin + f];
+    v = __double2float_rn(__dadd_rn(__dmul_rn(a.gin_ope, xs), (double)v));
+  }
+  if (a.bias) v = __fadd_rn(v, a.bias[f]);
+  return apply_act(v, a.act, a.act_param);
+}
+
+template <int V>
+struct VecT;
+template <>
+struct VecT<4> {
+  using T = float4;
+  static __device__ __forceinline__ T load(const float* p) {
+    return __ldg(reinterpret_cast<const float4*>(p));
+  }
+  static __device__ __forceinline__ float get(const T& v, int k) {
+    return k == 0 ? v.x : (k == 1 ? v.y : (k == 2 ? v.z : v.w));
+  }
+};
+template <>
+struct VecT<1> {
+  using T = float;
+  static __device__ __forceinline__ T load(const float* p) { return __ldg(p); }
+  static __device__ __forceinline__ float get(const T& v, int) { return v; }
+};
+
+// ---------------------------------------------------------------------------
+// light rows: G lanes per row
+// ---------------------------------------------------------------------------
+template <int OP, int V, int CH>
+__global__ void __launch_bounds__(256) k_agg_light(const AggArgs a, int G, int slice_w) {
+  // edges whose row data is in flight per lane: ~32 registers of staging
+  constexpr int U = (32 / (V * CH)) > 8 ? 8 : ((32 / (V * CH)) < 1 ? 1 : 32 / (V * CH));
+  using VT = typename VecT<V>::T;
+  const int lane = threadIdx.x & 31;
+  const int gl = lane & (G - 1);
+  const unsigned gmask = (G == 32) ? FULL : (((1u << G) - 1u) << (lane & ~(G - 1)));
+  const uint64_t gid = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) / (uint64_t)G;
+  if (gid >= a.n_rows) return;
+  const uint32_t row = (uint32_t)gid;
+  const uint32_t b = a.row_ptr[row];
+  const uint32_t deg = a.row_ptr[row + 1] - b;
+  if (deg >= a.heavy_threshold) return;  // the heavy-row kernel owns this row
+  const uint32_t total = deg + (a.tail ? 1u : 0u);
+  const int f_off = blockIdx.y * slice_w;
+  const int f_end = min(a.num_features, f_off + slice_w);
+  const int f0 = f_off + gl * V;
+
+  float acc[CH][V];
+#pragma unroll
+  for (int c = 0; c < CH; c++)
+#pragma unroll
+    for (int k = 0; k < V; k++) acc[c][k] = init_acc<OP>();
+  const float dinv_r = (OP == OP_GCN) ? a.dinv[row] : 0.0f;
+
+  for (uint32_t j0 = 0; j0 < total; j0 += G) {
+    const uint32_t jj = j0 + gl;
+    uint32_t my_s = row;
+    float my_w = 0.0f;
+    if (jj < deg) {
+      my_s = a.src_of[b + jj];
+      if (OP == OP_SPMM || OP == OP_SPMM_X) my_w = a.val[b + jj];
+    }
+    if (OP == OP_GCN && jj < total) my_w = __fmul_rn(a.dinv[my_s], dinv_r);
+    const int cnt = (int)min((uint32_t)G, total - j0);
+    for (int t = 0; t < cnt; t += U) {
+      VT buf[U][CH];
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        const uint32_t s = __shfl_sync(gmask, my_s, (t + u) & (G - 1), G);
+        const float* xr = a.x + (int64_t)s * a.ld_x;
+#pragma unroll
+        for (int c = 0; c < CH; c++) {
+          const int f = f0 + c * G * V;
+          if (t + u < cnt && f < f_end) buf[u][c] = VecT<V>::load(xr + f);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        const float w = __shfl_sync(gmask, my_w, (t + u) & (G - 1), G);
+        if (t + u < cnt) {
+#pragma unroll
+          for (int c = 0; c < CH; c++)
+#pragma unroll
+            for (int k = 0; k < V; k++) acc[c][k] = step<OP>(acc[c][k], VecT<V>::get(buf[u][c], k), w);
+        }
+      }
+    }
+  }
+  float* orow = a.out + (int64_t)row * a.ld_out;
+#pragma unroll
+  for (int c = 0; c < CH; c++) {
+    const int f = f0 + c * G * V;
+    if (f < f_end) {
+      if constexpr (V == 4) {
+        float4 o;
+        o.x = epilogue(acc[c][0], a, row, f + 0, total);
+        o.y = epilogue(acc[c][1], a, row, f + 1, total);
+        o.z = epilogue(acc[c][2], a, row, f + 2, total);
+        o.w = epilogue(acc[c][3], a, row, f + 3, total);
+        *reinterpret_cast<float4*>(orow + f) = o;
+      } else {
+        orow[f] = epilogue(acc[c][0], a, row, f, total);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// heavy rows: CTA per (row, 32-feature slice), cp.async ring
+// ---------------------------------------------------------------------------
+constexpr int HV_THREADS = 256;
+constexpr int HV_EPS = 128;    // edges per stage
+constexpr int HV_STAGES = 4;
+constexpr int HV_SW = 32;      // features per slice
+constexpr size_t HV_SMEM = (size_t)HV_STAGES * HV_EPS * (HV_SW + 1) * sizeof(float);
+
+__device__ __forceinline__ void cp_async16(void* s, const void* g) {
+  const unsigned sa = (unsigned)__cvta_generic_to_shared(s);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(sa), "l"(g) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* s, const void* g) {
+  const unsigned sa = (unsigned)__cvta_generic_to_shared(s);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(sa), "l"(g) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+template <int OP>
+__global__ void __launch_bounds__(HV_THREADS) k_agg_heavy(const AggArgs a, int vec4) {
+  extern __shared__ float4 hv_smem[];
+  float* buf = reinterpret_cast<float*>(hv_smem);          // [STAGES][EPS][SW]
+  float* wbuf = buf + (size_t)HV_STAGES * HV_EPS * HV_SW;  // [STAGES][EPS]
+  const uint32_t row = a.heavy_rows[blockIdx.x];
+  const int f0 = blockIdx.y * HV_SW;
+  if (f0 >= a.num_features) return;
+  const int fw = min(HV_SW, a.num_features - f0);
+  const uint32_t b = a.row_ptr[row];
+  const uint32_t deg = a.row_ptr[row + 1] - b;
+  const uint32_t total = deg + (a.tail ? 1u : 0u);
+  const uint32_t nst = (total + HV_EPS - 1) / HV_EPS;
+  const bool v4 = vec4 && (fw % 4 == 0);
+  const int per_edge = v4 ? fw / 4 : fw;
+  const int copies = HV_EPS * per_edge;
+  const float dinv_r = (OP == OP_GCN) ? a.dinv[row] : 0.0f;
+
+  auto issue = [&](uint32_t k) {
+    if (k < nst) {
+      const int st = (int)(k % HV_STAGES);
+      float* sb = buf + (size_t)st * HV_EPS * HV_SW;
+      float* wb = wbuf + (size_t)st * HV_EPS;
+      for (int c = threadIdx.x; c < copies; c += HV_THREADS) {
+        const int j = c / per_edge;
+        const int q = c - j * per_edge;
+        const uint32_t jj = k * HV_EPS + (uint32_t)j;
+        if (jj < total) {
+          const uint32_t s = jj < deg ? a.src_of[b + jj] : row;
+          const float* gp = a.x + (int64_t)s * a.ld_x + f0;
+          if (v4)
+            cp_async16(sb + j * HV_SW + 4 * q, gp + 4 * q);
+          else
+            cp_async4(sb + j * HV_SW + q, gp + q);
+          if (q == 0) {
+            if (OP == OP_GCN) cp_async4(wb + j, a.dinv + s);
+            if ((OP == OP_SPMM || OP == OP_SPMM_X) && jj < deg) cp_async4(wb + j, a.val + b + jj);
+          }
+        }
+      }
+    }
+    cp_async_commit();
+  };
+
+#pragma unroll
+  for (int k = 0; k < HV_STAGES - 1; k++) issue((uint32_t)k);
+  float acc = init_acc<OP>();
+  for (uint32_t k = 0; k < nst; k++) {
+    cp_async_wait<HV_STAGES - 2>();
+    __syncthreads();
+    issue(k + HV_STAGES - 1);
+    if (threadIdx.x < (unsigned)fw) {
+      const int st = (int)(k % HV_STAGES);
+      const float* sb = buf + (size_t)st * HV_EPS * HV_SW + threadIdx.x;
+      const float* wb = wbuf + (size_t)st * HV_EPS;
+      const uint32_t cnt = min((uint32_t)HV_EPS, total - k * HV_EPS);
+      for (uint32_t j = 0; j < cnt; j++) {
+        float w = 0.0f;
+        if (OP == OP_GCN) w = __fmul_rn(wb[j], dinv_r);
+        if (OP == OP_SPMM || OP == OP_SPMM_X) w = wb[j];
+        acc = step<OP>(acc, sb[j * HV_SW], w);
+      }
+    }
+  }
+  cp_async_wait<0>();
+  if (threadIdx.x < (unsigned)fw) {
+    const int f = f0 + threadIdx.x;
+    a.out[(int64_t)row * a.ld_out + f] = epilogue(acc, a, row, f, total);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host dispatch
+// ---------------------------------------------------------------------------
+template <int OP, int V, int CH>
+int launch_light(bgnn_ctx* ctx, const AggArgs& a, int G, int slices, int slice_w) {
+  const uint64_t threads = (uint64_t)a.n_rows * (uint64_t)G;
+  const uint64_t blocks = (threads + 255) / 256;
+  dim3 grid((unsigned)blocks, (unsigned)slices);
+  k_agg_light<OP, V, CH><<<grid, 256, 0, ctx->stream>>>(a, G, slice_w);
+  BGNN_LAUNCHED(ctx);
+  return BGNN_OK;
+}
+
+template <int OP, int V>
+int launch_light_ch(bgnn_ctx* ctx, const AggArgs& a, int G, int CH, int slices, int slice_w) {
+  switch (CH) {
+    case 1: return launch_light<OP, V, 1>(ctx, a, G, slices, slice_w);
+    case 2: return launch_light<OP, V, 2>(ctx, a, G, slices, slice_w);
+    case 4: return launch_light<OP, V, 4>(ctx, a, G, slices, slice_w);
+    default: return launch_light<OP, V, 8>(ctx, a, G, slices, slice_w);
+  }
+}
+
+template <int OP>
+int launch_heavy(bgnn_ctx* ctx, const AggArgs& a, int vec4, cudaStream_t s) {
+  BGNN_CUDA(ctx, cudaFuncSetAttribute(k_agg_heavy<OP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)HV_SMEM));
+  dim3 grid(a.n_heavy, (unsigned)((a.num_features + HV_SW - 1) / HV_SW));
+  k_agg_heavy<OP><<<grid, HV_THREADS, HV_SMEM, s>>>(a, vec4);
+  BGNN_LAUNCHED(ctx);
+  return BGNN_OK;
+}
+
+template <int OP>
+int run_op(bgnn_ctx* ctx, const AggArgs& a0) {
+  AggArgs a = a0;
+  const int F = a.num_features;
+  const bool al_x = ((uintptr_t)a.x % 16 == 0) && (a.ld_x % 4 == 0);
+  const bool al_o = ((uintptr_t)a.out % 16 == 0) && (a.ld_out % 4 == 0);
+  const int V = (F % 4 == 0 && al_x && al_o) ? 4 : 1;
+  const int nv = (F + V - 1) / V;
+  int G, CH, slices = 1, slice_w = F;
+  if (nv <= 32) {
+    G = 1;
+    while (G < nv) G <<= 1;
+    CH = 1;
+  } else if (nv <= 256) {
+    G = 32;
+    const int need = (nv + 31) / 32;
+    CH = need <= 2 ? 2 : (need <= 4 ? 4 : 8);
+  } else {
+    G = 32;
+    CH = 8;
+    slice_w = 256 * V;
+    slices = (F + slice_w - 1) / slice_w;
+  }
+  const bool heavy = a.n_heavy > 0 && a.heavy_rows != nullptr;
+  if (!heavy) a.heavy_threshold = 0xffffffffu;
+  if (heavy) {
+    BGNN_CUDA(ctx, cudaEventRecord(ctx->ev_fork, ctx->stream));
+    BGNN_CUDA(ctx, cudaStreamWaitEvent(ctx->aux_stream, ctx->ev_fork, 0));
+    BGNN_TRY(launch_heavy<OP>(ctx, a, al_x ? 1 : 0, ctx->aux_stream));
+    BGNN_CUDA(ctx, cudaEventRecord(ctx->ev_join, ctx->aux_stream));
+  }
+  int rc = (V == 4) ? launch_light_ch<OP, 4>(ctx, a, G, CH, slices, slice_w)
+                    : launch_light_ch<OP, 1>(ctx, a, G, CH, slices, slice_w);
+  if (heavy) BGNN_CUDA(ctx, cudaStreamWaitEvent(ctx->stream, ctx->ev_join, 0));
+  return rc;
+}
+
+}  // namespace
+
+int bgnn_run_aggregate(bgnn_ctx* ctx, int op, const AggArgs& a) {
+  if (a.n_rows == 0 || a.num_features == 0) return BGNN_OK;
+  switch (op) {
+    case OP_SUM: return run_op<OP_SUM>(ctx, a);
+    case OP_MAX: return run_op<OP_MAX>(ctx, a);
+    case OP_GCN: return run_op<OP_GCN>(ctx, a);
+    case OP_SPMM: return a.exact ? run_op<OP_SPMM_X>(ctx, a) : run_op<OP_SPMM>(ctx, a);
+    default: return bgnn_set_error(ctx, BGNN_ERR_INVALID_ARG, "unknown aggregation op %d", op);
+  }
+}

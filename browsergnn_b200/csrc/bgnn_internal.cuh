@@ -1,0 +1,210 @@
+// Internal declarations shared by the translation units of libbgnn_cuda.so.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include "bgnn.h"
+
+// ---------------------------------------------------------------------------
+// context and graph handles
+// ---------------------------------------------------------------------------
+struct bgnn_ctx {
+  int device = 0;
+  int num_sms = 148;
+  cudaStream_t stream = nullptr;      // stream all work is ordered on
+  cudaStream_t own_stream = nullptr;  // created by the context
+  cudaStream_t aux_stream = nullptr;  // heavy-row kernels run here, joined back
+  cudaEvent_t ev_fork = nullptr;
+  cudaEvent_t ev_join = nullptr;
+  int math = BGNN_MATH_FAST;
+  int* d_err = nullptr;      // [0]=code, [1]=info lo, [2]=info hi, [3]=where
+  uint32_t* d_small = nullptr;  // small device counters (heavy-row count etc.)
+  uint64_t launches = 0;
+  std::string last_error;
+};
+
+struct bgnn_graph {
+  int device = 0;
+  uint32_t n_src = 0, n_dst = 0;
+  uint64_t num_edges = 0;
+  uint32_t* row_ptr = nullptr;     // [n_dst+1] destination-keyed CSR
+  uint32_t* src_of = nullptr;      // [E] source node of each CSR slot
+  uint32_t* eid = nullptr;         // [E] COO edge id of each CSR slot
+  uint32_t* out_deg = nullptr;     // [n_src]
+  uint32_t* heavy_rows = nullptr;  // rows handled CTA-per-row
+  uint32_t n_heavy = 0;
+  uint32_t heavy_threshold = 0;
+  int has_self_loops = 0;
+  bool csr_only = false;           // built from an existing CSR (no eid/out_deg)
+  float* dinv[2] = {nullptr, nullptr};  // GCN D^-1/2 without / with loop tail
+};
+
+// ---------------------------------------------------------------------------
+// error plumbing: every internal call returns a bgnn_status
+// ---------------------------------------------------------------------------
+int bgnn_set_error(bgnn_ctx* ctx, int code, const char* fmt, ...);
+
+#define BGNN_CUDA(ctx, call)                                                       \
+  do {                                                                             \
+    cudaError_t _e = (call);                                                       \
+    if (_e != cudaSuccess) {                                                       \
+      return bgnn_set_error((ctx), _e == cudaErrorMemoryAllocation ? BGNN_ERR_NO_MEMORY \
+                                                                   : BGNN_ERR_CUDA, \
+                            "%s failed: %s (%s:%d)", #call, cudaGetErrorString(_e),  \
+                            __FILE__, __LINE__);                                   \
+    }                                                                              \
+  } while (0)
+
+#define BGNN_LAUNCHED(ctx)                                                         \
+  do {                                                                             \
+    cudaError_t _e = cudaGetLastError();                                           \
+    if (_e != cudaSuccess)                                                         \
+      return bgnn_set_error((ctx), BGNN_ERR_CUDA, "kernel launch failed: %s (%s:%d)", \
+                            cudaGetErrorString(_e), __FILE__, __LINE__);           \
+    (ctx)->launches++;                                                             \
+  } while (0)
+
+#define BGNN_TRY(x)              \
+  do {                           \
+    int _s = (x);                \
+    if (_s != BGNN_OK) return _s; \
+  } while (0)
+
+#define BGNN_REQUIRE(ctx, cond, ...)                                   \
+  do {                                                                 \
+    if (!(cond)) return bgnn_set_error((ctx), BGNN_ERR_INVALID_ARG, __VA_ARGS__); \
+  } while (0)
+
+// Stream-ordered temporary device buffer (cudaMallocAsync on the ctx stream).
+struct DevTmp {
+  void* p = nullptr;
+  cudaStream_t s = nullptr;
+  DevTmp() = default;
+  DevTmp(const DevTmp&) = delete;
+  DevTmp& operator=(const DevTmp&) = delete;
+  ~DevTmp() {
+    if (p) cudaFreeAsync(p, s);
+  }
+  template <class T>
+  T* as() const {
+    return static_cast<T*>(p);
+  }
+};
+int bgnn_tmp_alloc(bgnn_ctx* ctx, DevTmp& t, size_t bytes);
+
+// device error word codes (written by kernels, read at synchronisation)
+enum : int { DEVERR_NONE = 0, DEVERR_INDEX = 1, DEVERR_TIMEOUT = 2 };
+
+__device__ __forceinline__ void dev_raise(int* err, int code, uint64_t info, int where) {
+  if (atomicCAS(err, 0, code) == 0) {
+    err[1] = (int)(uint32_t)(info & 0xffffffffu);
+    err[2] = (int)(uint32_t)(info >> 32);
+    err[3] = where;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// primitives (util.cu)
+// ---------------------------------------------------------------------------
+// exclusive prefix sum of n uint32 values (in may equal out)
+int bgnn_exclusive_scan(bgnn_ctx* ctx, const uint32_t* in, uint32_t* out, uint64_t n);
+// stable LSD radix sort of 32-bit keys carrying 32-bit values.  vals_in NULL
+// means the identity (0,1,2,...).  key_bits: number of low key bits to sort.
+// Results land in keys_out / vals_out (keys_out may be NULL when only the
+// permutation is wanted).
+int bgnn_radix_sort_pairs(bgnn_ctx* ctx, const uint32_t* keys_in, const uint32_t* vals_in,
+                          uint64_t n, int key_bits, uint32_t* keys_out, uint32_t* vals_out);
+int bgnn_bits_for(uint64_t max_value);
+// out[i] = src[idx[i]]
+int bgnn_gather_u32(bgnn_ctx* ctx, const uint32_t* src, const uint32_t* idx, uint64_t n,
+                    uint32_t* out);
+int bgnn_gather_f32(bgnn_ctx* ctx, const float* src, const uint32_t* idx, uint64_t n, float* out);
+int bgnn_iota(bgnn_ctx* ctx, uint32_t* out, uint64_t n);
+int bgnn_check_device_error(bgnn_ctx* ctx);
+
+// ---------------------------------------------------------------------------
+// graph construction (graph.cu)
+// ---------------------------------------------------------------------------
+int bgnn_graph_build(bgnn_ctx* ctx, const uint32_t* src_dev, const uint32_t* dst_dev,
+                     uint64_t num_edges, uint32_t num_src, uint32_t num_dst, bgnn_graph* g);
+int bgnn_graph_from_csr(bgnn_ctx* ctx, const uint32_t* row_ptr, const uint32_t* col,
+                        uint32_t num_rows, uint32_t num_cols, bgnn_graph* g, bool copy);
+void bgnn_graph_free(bgnn_graph* g);
+int bgnn_graph_dinv(bgnn_ctx* ctx, bgnn_graph* g, int tail, const float** out);
+
+// ---------------------------------------------------------------------------
+// aggregation (aggregate.cu)
+// ---------------------------------------------------------------------------
+enum AggOp : int { OP_SUM = 0, OP_MAX = 1, OP_GCN = 2, OP_SPMM = 3 };
+
+struct AggArgs {
+  const uint32_t* row_ptr;
+  const uint32_t* src_of;
+  const float* x;
+  int64_t ld_x;
+  const float* val;       // OP_SPMM: per-slot values
+  const float* dinv;      // OP_GCN: per-node D^-1/2
+  uint32_t n_rows;
+  int num_features;
+  float* out;
+  int64_t ld_out;
+  const uint32_t* heavy_rows;
+  uint32_t n_heavy;
+  uint32_t heavy_threshold;
+  int tail;               // virtual self-loop edge after each row's edges
+  int mean;               // sum * (1/count)
+  int max_fix;            // -inf -> 0
+  const float* bias;
+  const float* gin_x;     // GIN combine: out = (1+eps)*x_self + agg
+  int64_t ld_gin;
+  double gin_ope;
+  int act;
+  double act_param;
+  int exact;              // OP_SPMM rounding mode
+};
+int bgnn_run_aggregate(bgnn_ctx* ctx, int op, const AggArgs& a);
+
+// ---------------------------------------------------------------------------
+// GAT (gat.cu)
+// ---------------------------------------------------------------------------
+int bgnn_run_gat(bgnn_ctx* ctx, const bgnn_graph* g, const float* h, uint32_t heads, uint32_t c,
+                 const float* att_src, const float* att_dst, double slope, int concat, int tail,
+                 const float* bias, int act, double act_param, float* out);
+
+// ---------------------------------------------------------------------------
+// dense (gemm.cu)
+// ---------------------------------------------------------------------------
+int bgnn_run_linear(bgnn_ctx* ctx, const float* a, const float* w, const float* a2,
+                    const float* w2, uint32_t m, uint32_t k, uint32_t n, const float* bias,
+                    int act, double act_param, float* out);
+int bgnn_run_activation(bgnn_ctx* ctx, int act, double param, const float* x, uint64_t n,
+                        float* out);
+int bgnn_run_add(bgnn_ctx* ctx, const float* a, const float* b, uint64_t n, float* out);
+int bgnn_run_l2norm(bgnn_ctx* ctx, float* x, uint32_t m, uint32_t n);
+int bgnn_run_gather_rows(bgnn_ctx* ctx, const float* x, uint32_t num_x_rows,
+                         const uint32_t* idx, uint64_t n, uint32_t f, float* out);
+int bgnn_run_spmv(bgnn_ctx* ctx, const uint32_t* row_ptr, const uint32_t* col,
+                  const float* val, const float* x, uint32_t num_rows, float* out);
+
+// ---------------------------------------------------------------------------
+// shared device helpers: the reference's activations and f32 store points
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float apply_act(float v, int act, double p) {
+  switch (act) {
+    case BGNN_ACT_RELU:  // wasmRelu: x > 0 ? x : 0 (NaN -> 0)
+      return v > 0.0f ? v : 0.0f;
+    case BGNN_ACT_RELU_MAX:  // Math.max(0, x): NaN propagates, -0 -> +0
+      return (v != v) ? v : (v > 0.0f ? v : 0.0f);
+    case BGNN_ACT_ELU:  // x > 0 ? x : alpha*(exp(x)-1), evaluated in double
+      return v > 0.0f ? v : __double2float_rn(__dmul_rn(p, __dsub_rn(exp((double)v), 1.0)));
+    case BGNN_ACT_LEAKY_RELU:
+      return v > 0.0f ? v : __double2float_rn(__dmul_rn(p, (double)v));
+    default:
+      return v;
+  }
+}

@@ -1,0 +1,308 @@
+// Dense transforms and elementwise ops with the reference's rounding.
+//
+// X*W (wasmMatmul, src/backend/wasm/index.ts:18-63): for every output (i,j)
+// the reference runs k = 0..K-1 in ascending order and stores
+// f32(acc + a*b) (double arithmetic) after each step.  The kernel keeps that
+// order: each output is owned by one thread that walks k ascending.
+//   BGNN_MATH_EXACT: f64 fma (the product of two floats is exact in double)
+//                    then one rounding to f32 -- the reference's bits.
+//   BGNN_MATH_FAST:  f32 fma in the same order; differs from the reference
+//                    only where its double result lands on an f32 tie.
+// K tails are not zero-padded (an extra fma with 0 could turn a -0 into +0).
+// The SAGE variant accumulates X*W_self and Agg*W_neigh in one pass and
+// stores f32(self + neigh) (Tensor.add -> wasmAdd, sage.ts:178-183).
+#include "bgnn_internal.cuh"
+
+namespace {
+
+struct GemmArgs {
+  const float* a;   // [m, k]
+  const float* b;   // [k, n]
+  const float* a2;  // second product (SAGE), same shapes
+  const float* b2;
+  const float* bias;
+  float* out;       // [m, n]
+  uint32_t m, k, n;
+  int act;
+  double act_param;
+};
+
+template <bool EXACT>
+__device__ __forceinline__ float mac(float a, float b, float acc) {
+  if constexpr (EXACT) {
+    return __double2float_rn(__fma_rn((double)a, (double)b, (double)acc));
+  } else {
+    return __fmaf_rn(a, b, acc);
+  }
+}
+
+template <int BM, int BN, int TM, int TN, bool EXACT, bool DUAL>
+__global__ void __launch_bounds__(256) k_gemm(const GemmArgs g) {
+  constexpr int BK = 8;
+  constexpr int TX = BN / TN;
+  static_assert((BM / TM) * (BN / TN) == 256, "256 threads per tile");
+  constexpr int A_PER = BM * BK / 256;
+  constexpr int B_PER = (BK * BN + 255) / 256;
+  constexpr int NA = DUAL ? 2 : 1;
+  __shared__ __align__(16) float As[NA][2][BK][BM];
+  __shared__ __align__(16) float Bs[NA][2][BK][BN];
+  const int tid = threadIdx.x;
+  const int tx = tid % TX, ty = tid / TX;
+  const uint64_t m0 = (uint64_t)blockIdx.x * BM;
+  const uint32_t n0 = blockIdx.y * BN;
+  const float* A[2] = {g.a, g.a2};
+  const float* B[2] = {g.b, g.b2};
+
+  float acc[NA][TM][TN];
+#pragma unroll
+  for (int p = 0; p < NA; p++)
+#pragma unroll
+    for (int i = 0; i < TM; i++)
+#pragma unroll
+      for (int j = 0; j < TN; j++) acc[p][i][j] = 0.0f;
+
+  float ra[NA][A_PER], rb[NA][B_PER];
+  auto load_tile = [&](uint32_t k0) {
+#pragma unroll
+    for (int p = 0; p < NA; p++) {
+#pragma unroll
+      for (int i = 0; i < A_PER; i++) {
+        const int idx = tid + i * 256;
+        const int r = idx / BK, kk = idx % BK;
+        const uint64_t gm = m0 + r;
+        const uint32_t gk = k0 + kk;
+        ra[p][i] = (gm < g.m && gk < g.k) ? __ldg(A[p] + gm * g.k + gk) : 0.0f;
+      }
+#pragma unroll
+      for (int i = 0; i < B_PER; i++) {
+        const int idx = tid + i * 256;
+        const int kk = idx / BN, c = idx % BN;
+        const uint32_t gk = k0 + kk, gn = n0 + c;
+        rb[p][i] = (idx < BK * BN && gk < g.k && gn < g.n) ? __ldg(B[p] + (uint64_t)gk * g.n + gn)
+                                                            : 0.0f;
+      }
+    }
+  };
+  auto store_tile = [&](int buf) {
+#pragma unroll
+    for (int p = 0; p < NA; p++) {
+#pragma unroll
+      for (int i = 0; i < A_PER; i++) {
+        const int idx = tid + i * 256;
+        As[p][buf][idx % BK][idx / BK] = ra[p][i];
+      }
+#pragma unroll
+      for (int i = 0; i < B_PER; i++) {
+        const int idx = tid + i * 256;
+        if (idx < BK * BN) Bs[p][buf][idx / BN][idx % BN] = rb[p][i];
+      }
+    }
+  };
+
+  const uint32_t ntiles = (g.k + BK - 1) / BK;
+  load_tile(0);
+  store_tile(0);
+  __syncthreads();
+  for (uint32_t t = 0; t < ntiles; t++) {
+    const int cur = t & 1;
+    if (t + 1 < ntiles) load_tile((t + 1) * BK);
+    const int kmax = (int)min((uint32_t)BK, g.k - t * BK);
+#pragma unroll
+    for (int kk = 0; kk < BK; kk++) {
+      if (kk < kmax) {
+#pragma unroll
+        for (int p = 0; p < NA; p++) {
+          float av[TM], bv[TN];
+#pragma unroll
+          for (int i = 0; i < TM; i++) av[i] = As[p][cur][kk][ty * TM + i];
+#pragma unroll
+          for (int j = 0; j < TN; j++) bv[j] = Bs[p][cur][kk][tx * TN + j];
+#pragma unroll
+          for (int i = 0; i < TM; i++)
+#pragma unroll
+            for (int j = 0; j < TN; j++) acc[p][i][j] = mac<EXACT>(av[i], bv[j], acc[p][i][j]);
+        }
+      }
+    }
+    if (t + 1 < ntiles) store_tile(cur ^ 1);
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < TM; i++) {
+    const uint64_t gm = m0 + ty * TM + i;
+    if (gm >= g.m) continue;
+#pragma unroll
+    for (int j = 0; j < TN; j++) {
+      const uint32_t gn = n0 + tx * TN + j;
+      if (gn >= g.n) continue;
+      float v = acc[0][i][j];
+      if constexpr (DUAL) v = __fadd_rn(acc[1][i][j], acc[0][i][j]);
+      if (g.bias) v = __fadd_rn(v, g.bias[gn]);
+      g.out[gm * g.n + gn] = apply_act(v, g.act, g.act_param);
+    }
+  }
+}
+
+template <int BM, int BN, int TM, int TN, bool EXACT, bool DUAL>
+int launch_gemm(bgnn_ctx* ctx, const GemmArgs& g) {
+  dim3 grid((unsigned)((g.m + BM - 1) / BM), (g.n + BN - 1) / BN);
+  k_gemm<BM, BN, TM, TN, EXACT, DUAL><<<grid, 256, 0, ctx->stream>>>(g);
+  BGNN_LAUNCHED(ctx);
+  return BGNN_OK;
+}
+
+template <bool EXACT, bool DUAL>
+int pick_tile(bgnn_ctx* ctx, const GemmArgs& g) {
+  if (g.n <= 16) return launch_gemm<256, 16, 4, 4, EXACT, DUAL>(ctx, g);
+  return launch_gemm<128, 64, 8, 4, EXACT, DUAL>(ctx, g);
+}
+
+// ---- elementwise -----------------------------------------------------------
+__global__ void k_act(int act, double p, const float* __restrict__ x, uint64_t n,
+                      float* __restrict__ out) {
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (uint64_t)gridDim.x * blockDim.x)
+    out[i] = apply_act(x[i], act, p);
+}
+
+__global__ void k_add(const float* __restrict__ a, const float* __restrict__ b, uint64_t n,
+                      float* __restrict__ out) {
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (uint64_t)gridDim.x * blockDim.x)
+    out[i] = __fadd_rn(a[i], b[i]);
+}
+
+// SAGE L2 normalise (sage.ts:199-214): norm = sqrt(sum v*v) in double,
+// sequential over the row; out = f32(v / norm) when norm > 0.
+__global__ void k_l2norm(float* x, uint32_t m, uint32_t n) {
+  for (uint32_t r = blockIdx.x * blockDim.x + threadIdx.x; r < m; r += gridDim.x * blockDim.x) {
+    float* row = x + (uint64_t)r * n;
+    double s = 0.0;
+    for (uint32_t f = 0; f < n; f++) {
+      const double v = (double)row[f];
+      s = __dadd_rn(s, __dmul_rn(v, v));
+    }
+    const double nrm = __dsqrt_rn(s);
+    if (nrm > 0.0)
+      for (uint32_t f = 0; f < n; f++) row[f] = __double2float_rn(__ddiv_rn((double)row[f], nrm));
+  }
+}
+
+__global__ void k_gather_rows(const float* __restrict__ x, uint32_t nx,
+                              const uint32_t* __restrict__ idx, uint64_t n, uint32_t f,
+                              float* __restrict__ out, int* err) {
+  const uint64_t total = n * f;
+  for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+       t += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t i = t / f;
+    const uint32_t c = (uint32_t)(t - i * f);
+    const uint32_t s = idx[i];
+    if (s >= nx) {
+      if (c == 0) dev_raise(err, DEVERR_INDEX, i, 1);
+      out[t] = 0.0f;
+    } else {
+      out[t] = x[(uint64_t)s * f + c];
+    }
+  }
+}
+
+// wasmSpmv (index.ts:304-335): double accumulator, one rounding at the store
+__global__ void k_spmv(const uint32_t* __restrict__ rp, const uint32_t* __restrict__ col,
+                       const float* __restrict__ val, const float* __restrict__ x, uint32_t rows,
+                       float* __restrict__ out) {
+  for (uint32_t r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x) {
+    double s = 0.0;
+    for (uint32_t j = rp[r]; j < rp[r + 1]; j++)
+      s = __dadd_rn(s, __dmul_rn((double)val[j], (double)x[col[j]]));
+    out[r] = __double2float_rn(s);
+  }
+}
+
+// SAGE pool projection (sage.ts:149-159): sum = bias[j] + sum_k x*w with a
+// double accumulator (no per-step f32 store), stored as f32(Math.max(0, sum)).
+__global__ void k_pool_proj(const float* __restrict__ x, const float* __restrict__ w,
+                            const float* __restrict__ b, uint32_t m, uint32_t k,
+                            float* __restrict__ out) {
+  const uint64_t total = (uint64_t)m * k;
+  for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+       t += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t i = t / k;
+    const uint32_t j = (uint32_t)(t - i * k);
+    double s = b ? (double)b[j] : 0.0;
+    const float* xr = x + i * k;
+    for (uint32_t q = 0; q < k; q++) s = __dadd_rn(s, __dmul_rn((double)xr[q], (double)w[(uint64_t)q * k + j]));
+    out[t] = (s != s) ? __double2float_rn(s) : (s > 0.0 ? __double2float_rn(s) : 0.0f);
+  }
+}
+
+inline unsigned grid_for(bgnn_ctx* ctx, uint64_t n, int tpb) {
+  uint64_t b = (n + tpb - 1) / tpb;
+  const uint64_t cap = (uint64_t)ctx->num_sms * 16;
+  if (b > cap) b = cap;
+  if (b == 0) b = 1;
+  return (unsigned)b;
+}
+
+}  // namespace
+
+int bgnn_run_linear(bgnn_ctx* ctx, const float* a, const float* w, const float* a2,
+                    const float* w2, uint32_t m, uint32_t k, uint32_t n, const float* bias,
+                    int act, double act_param, float* out) {
+  if (m == 0 || n == 0) return BGNN_OK;
+  // k == 0 runs no mac step: the output is act(0 + bias), as in the reference
+  GemmArgs g{a, w, a2, w2, bias, out, m, k, n, act, act_param};
+  const bool dual = a2 != nullptr && w2 != nullptr;
+  const bool exact = ctx->math == BGNN_MATH_EXACT;
+  if (exact) return dual ? pick_tile<true, true>(ctx, g) : pick_tile<true, false>(ctx, g);
+  return dual ? pick_tile<false, true>(ctx, g) : pick_tile<false, false>(ctx, g);
+}
+
+int bgnn_run_activation(bgnn_ctx* ctx, int act, double param, const float* x, uint64_t n,
+                        float* out) {
+  if (n == 0) return BGNN_OK;
+  k_act<<<grid_for(ctx, n, 256), 256, 0, ctx->stream>>>(act, param, x, n, out);
+  BGNN_LAUNCHED(ctx);
+  return BGNN_OK;
+}
+
+int bgnn_run_add(bgnn_ctx* ctx, const float* a, const float* b, uint64_t n, float* out) {
+  if (n == 0) return BGNN_OK;
+  k_add<<<grid_for(ctx, n, 256), 256, 0, ctx->stream>>>(a, b, n, out);
+  BGNN_LAUNCHED(ctx);
+  return BGNN_OK;
+}
+
+int bgnn_run_l2norm(bgnn_ctx* ctx, float* x, uint32_t m, uint32_t n) {
+  if (m == 0 || n == 0) return BGNN_OK;
+  k_l2norm<<<grid_for(ctx, m, 128), 128, 0, ctx->stream>>>(x, m, n);
+  BGNN_LAUNCHED(ctx);
+  return BGNN_OK;
+}
+
+int bgnn_run_gather_rows(bgnn_ctx* ctx, const float* x, uint32_t nx, const uint32_t* idx,
+                         uint64_t n, uint32_t f, float* out) {
+  if (n == 0 || f == 0) return BGNN_OK;
+  k_gather_rows<<<grid_for(ctx, n * f, 256), 256, 0, ctx->stream>>>(x, nx, idx, n, f, out,
+                                                                      ctx->d_err);
+  BGNN_LAUNCHED(ctx);
+  return BGNN_OK;
+}
+
+int bgnn_run_spmv(bgnn_ctx* ctx, const uint32_t* row_ptr, const uint32_t* col, const float* val,
+                  const float* x, uint32_t num_rows, float* out) {
+  if (num_rows == 0) return BGNN_OK;
+  k_spmv<<<grid_for(ctx, num_rows, 128), 128, 0, ctx->stream>>>(row_ptr, col, val, x, num_rows, out);
+  BGNN_LAUNCHED(ctx);
+  return BGNN_OK;
+}
+
+extern "C" int bgnn_pool_projection(bgnn_ctx* ctx, const float* x, const float* w,
+                                    const float* bias, uint32_t m, uint32_t k, float* out) {
+  if (!ctx) return BGNN_ERR_INVALID_ARG;
+  BGNN_CUDA(ctx, cudaSetDevice(ctx->device));
+  BGNN_REQUIRE(ctx, (x && w && out) || (uint64_t)m * k == 0, "NULL argument");
+  if ((uint64_t)m * k == 0) return BGNN_OK;
+  k_pool_proj<<<grid_for(ctx, (uint64_t)m * k, 256), 256, 0, ctx->stream>>>(x, w, bias, m, k, out);
+  BGNN_LAUNCHED(ctx);
+  return BGNN_OK;
+}

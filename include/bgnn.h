@@ -1,0 +1,252 @@
+/*
+ * bgnn.h -- C ABI of libbgnn_cuda.so, the sm_100a (B200) backend for
+ * BrowserGNN's message-passing path.
+ *
+ * The reference's device boundary is the GPUSparse / GPUTensor facade over
+ * WebGPUComputeManager (src/core/gpu-sparse.ts:19-285,
+ * src/backend/webgpu/compute-pipeline.ts:140-644).  Each entry point below
+ * names the reference method it replaces.  Two families:
+ *
+ *   *_host  the reference's ownership model: the caller keeps its host
+ *           buffers, the library copies inputs in, computes, copies the result
+ *           into a caller-allocated host buffer and returns when it is there
+ *           (WebGPUComputeManager uploads, dispatches and reads back per op).
+ *   *_dev   device pointers, asynchronous on the context's stream, for
+ *           device-resident multi-layer pipelines.  Results are ready after
+ *           bgnn_ctx_synchronize (or any later operation on the same stream).
+ *
+ * Conventions: every call returns a bgnn_status; no exception or abort
+ * crosses the ABI; bgnn_last_error() describes the last failure on a context.
+ * A context is used by one host thread at a time.  Outputs are always
+ * caller-allocated.  Feature matrices are row-major float32 [rows, features];
+ * indices are uint32 node ids; edge_index is the reference's flat layout
+ * [sources(E) | targets(E)] (src/core/graph.ts:14-35).
+ *
+ * Arithmetic: the reference evaluates in IEEE double and rounds once to f32
+ * at every Float32Array store; the kernels reproduce that rounding sequence.
+ * Sum/mean/max aggregation, GCN propagation, scatter/gather, CSR/degree/norm
+ * construction are bit-exact with the reference in both math modes.  With
+ * BGNN_MATH_EXACT the dense X*W transform and the SpMM/GAT accumulations are
+ * bit-exact too (f64 emulation of each JS step); BGNN_MATH_FAST (default)
+ * uses f32 FMA in the same order, which differs only where the reference's
+ * double rounding lands on an f32 tie (well inside 1e-5 rel / 1e-6 abs).
+ */
+#ifndef BGNN_H
+#define BGNN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BGNN_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define BGNN_API __attribute__((visibility("default")))
+#else
+#define BGNN_API
+#endif
+
+typedef enum bgnn_status {
+  BGNN_OK = 0,
+  BGNN_ERR_INVALID_ARG = 1,   /* bad size, null pointer, shape mismatch      */
+  BGNN_ERR_OUT_OF_RANGE = 2,  /* an index >= its bound (graph.ts:88-92)      */
+  BGNN_ERR_CUDA = 3,          /* a CUDA runtime call failed                  */
+  BGNN_ERR_NO_MEMORY = 4,     /* device allocation failed                    */
+  BGNN_ERR_TIMEOUT = 5,       /* a bounded device wait gave up               */
+  BGNN_ERR_UNSUPPORTED = 6,   /* configuration the backend does not provide  */
+  BGNN_ERR_DEVICE = 7         /* a kernel raised its error flag              */
+} bgnn_status;
+
+typedef enum bgnn_math_mode { BGNN_MATH_FAST = 0, BGNN_MATH_EXACT = 1 } bgnn_math_mode;
+
+typedef enum bgnn_aggr {
+  BGNN_AGGR_SUM = 0,  /* wasmScatterAdd  src/backend/wasm/index.ts:70-105  */
+  BGNN_AGGR_MEAN = 1, /* wasmScatterMean src/backend/wasm/index.ts:112-151 */
+  BGNN_AGGR_MAX = 2   /* wasmScatterMax  src/backend/wasm/index.ts:158-206 */
+} bgnn_aggr;
+
+typedef enum bgnn_act {
+  BGNN_ACT_NONE = 0,
+  BGNN_ACT_RELU = 1,       /* wasmRelu: x > 0 ? x : 0   (index.ts:250-271)  */
+  BGNN_ACT_RELU_MAX = 2,   /* Math.max(0, x): NaN kept  (gin.ts:106-112)    */
+  BGNN_ACT_ELU = 3,        /* x > 0 ? x : a*(exp(x)-1)  (activation.ts:56-65) */
+  BGNN_ACT_LEAKY_RELU = 4  /* x > 0 ? x : s*x           (tensor.ts:401-408) */
+} bgnn_act;
+
+typedef struct bgnn_ctx bgnn_ctx;
+typedef struct bgnn_graph bgnn_graph;
+
+/* ---- context ------------------------------------------------------------ */
+BGNN_API int bgnn_abi_version(void);
+/* Replaces BackendManager.initialize / initWebGPU (src/backend/index.ts:102-182). */
+BGNN_API int bgnn_ctx_create(int device, bgnn_ctx** out);
+BGNN_API int bgnn_ctx_destroy(bgnn_ctx* ctx);
+/* Run subsequent work on an existing cudaStream_t (NULL: the legacy default
+ * stream).  A new context starts on a non-blocking stream of its own. */
+BGNN_API int bgnn_ctx_set_stream(bgnn_ctx* ctx, void* cuda_stream);
+BGNN_API int bgnn_ctx_set_math(bgnn_ctx* ctx, int math_mode);
+/* Waits for the context's stream and reports any kernel-raised error. */
+BGNN_API int bgnn_ctx_synchronize(bgnn_ctx* ctx);
+BGNN_API const char* bgnn_last_error(const bgnn_ctx* ctx);
+/* Count of this library's kernel launches on the context (for accounting). */
+BGNN_API uint64_t bgnn_ctx_launch_count(const bgnn_ctx* ctx);
+
+/* ---- facade mirror: WebGPUComputeManager methods, host buffers ---------- */
+/* spmm: compute-pipeline.ts:140-232 / wasmSpmm index.ts:342-383 */
+BGNN_API int bgnn_spmm_host(bgnn_ctx* ctx, const uint32_t* row_ptr, const uint32_t* col_indices,
+                   const float* values, const float* dense, uint32_t num_rows,
+                   uint32_t num_cols, uint32_t num_features, float* out);
+/* scatterAdd: compute-pipeline.ts:237-305 / wasmScatterAdd index.ts:70-105 */
+BGNN_API int bgnn_scatter_add_host(bgnn_ctx* ctx, const float* src, const uint32_t* index,
+                          uint64_t num_msgs, uint32_t num_nodes, uint32_t num_features,
+                          float* out);
+/* scatterMean: gpu-sparse.ts:113-122 (CPU-only there) / index.ts:112-151 */
+BGNN_API int bgnn_scatter_mean_host(bgnn_ctx* ctx, const float* src, const uint32_t* index,
+                           uint64_t num_msgs, uint32_t num_nodes, uint32_t num_features,
+                           float* out);
+/* scatterMax: compute-pipeline.ts:310-385 / index.ts:158-206 */
+BGNN_API int bgnn_scatter_max_host(bgnn_ctx* ctx, const float* src, const uint32_t* index,
+                          uint64_t num_msgs, uint32_t num_nodes, uint32_t num_features,
+                          float* out);
+/* gather: compute-pipeline.ts:390-453 / index.ts:213-245 */
+BGNN_API int bgnn_gather_host(bgnn_ctx* ctx, const float* src, uint32_t num_src_rows,
+                     const uint32_t* index, uint64_t num_idx, uint32_t num_features,
+                     float* out);
+/* matmul: compute-pipeline.ts:458-521 / wasmMatmul index.ts:18-63 */
+BGNN_API int bgnn_matmul_host(bgnn_ctx* ctx, const float* a, const float* b, uint32_t m, uint32_t k,
+                     uint32_t n, float* out);
+/* relu: compute-pipeline.ts:526-576 / index.ts:250-271 */
+BGNN_API int bgnn_relu_host(bgnn_ctx* ctx, const float* x, uint64_t n, float* out);
+/* add: compute-pipeline.ts:581-644 / index.ts:276-297 */
+BGNN_API int bgnn_add_host(bgnn_ctx* ctx, const float* a, const float* b, uint64_t n, float* out);
+/* wasmSpmv index.ts:304-335 (SparseCSR.matvec sparse.ts:301-317) */
+BGNN_API int bgnn_spmv_host(bgnn_ctx* ctx, const uint32_t* row_ptr, const uint32_t* col_indices,
+                   const float* values, const float* x, uint32_t num_rows, uint32_t num_cols,
+                   float* out);
+
+/* ---- the same ops on device pointers (async on the context stream) ------ */
+BGNN_API int bgnn_spmm_dev(bgnn_ctx* ctx, const uint32_t* row_ptr, const uint32_t* col_indices,
+                  const float* values, const float* dense, uint32_t num_rows,
+                  uint32_t num_cols, uint32_t num_features, float* out);
+BGNN_API int bgnn_scatter_dev(bgnn_ctx* ctx, int aggr, const float* src, const uint32_t* index,
+                     uint64_t num_msgs, uint32_t num_nodes, uint32_t num_features, float* out);
+BGNN_API int bgnn_gather_dev(bgnn_ctx* ctx, const float* src, uint32_t num_src_rows,
+                    const uint32_t* index, uint64_t num_idx, uint32_t num_features, float* out);
+BGNN_API int bgnn_matmul_dev(bgnn_ctx* ctx, const float* a, const float* b, uint32_t m, uint32_t k,
+                    uint32_t n, float* out);
+/* out[i] = act(x[i]); param = ELU alpha or LeakyReLU slope */
+BGNN_API int bgnn_activation_dev(bgnn_ctx* ctx, int act, double param, const float* x, uint64_t n,
+                        float* out);
+BGNN_API int bgnn_add_dev(bgnn_ctx* ctx, const float* a, const float* b, uint64_t n, float* out);
+BGNN_API int bgnn_spmv_dev(bgnn_ctx* ctx, const uint32_t* row_ptr, const uint32_t* col_indices,
+                  const float* values, const float* x, uint32_t num_rows, uint32_t num_cols,
+                  float* out);
+
+/* ---- COO -> CSR, degrees, normalisation (device pointers) -------------- */
+/* SparseCSR.fromCOO (src/core/sparse.ts:259-296): stable sort by (row, col),
+ * bit-exact.  values may be NULL (all ones, SparseCOO.fromEdgeIndex
+ * sparse.ts:81-92); val_out may be NULL. */
+BGNN_API int bgnn_coo_to_csr_dev(bgnn_ctx* ctx, const uint32_t* rows, const uint32_t* cols,
+                        const float* values, uint64_t nnz, uint32_t num_rows, uint32_t num_cols,
+                        uint32_t* row_ptr, uint32_t* col_out, float* val_out);
+BGNN_API int bgnn_coo_to_csr_host(bgnn_ctx* ctx, const uint32_t* rows, const uint32_t* cols,
+                         const float* values, uint64_t nnz, uint32_t num_rows,
+                         uint32_t num_cols, uint32_t* row_ptr, uint32_t* col_out,
+                         float* val_out);
+/* computeGCNNorm (src/core/sparse.ts:480-513): per-edge f32 weights. */
+BGNN_API int bgnn_gcn_norm_dev(bgnn_ctx* ctx, const uint32_t* edge_index, uint64_t num_edges,
+                      uint32_t num_nodes, int add_self_loops, float* out);
+
+/* ---- device-resident graph (cached destination CSR) -------------------- */
+/* Validates indices like the GraphData constructor (src/core/graph.ts:88-92),
+ * then builds once: the destination-keyed CSR with each row's edges in COO
+ * order (stable), in/out degrees, the self-loop flag (graph.ts:220-227) and
+ * the row schedule.  edge_index is [src(E) | dst(E)], on the host when
+ * edge_index_on_host != 0, else on the device.  num_src == num_dst for an
+ * ordinary graph; a partition's local graph has num_dst owned rows and
+ * num_src = owned + halo columns. */
+BGNN_API int bgnn_graph_create(bgnn_ctx* ctx, const uint32_t* edge_index, uint64_t num_edges,
+                      uint32_t num_src, uint32_t num_dst, int edge_index_on_host,
+                      bgnn_graph** out);
+/* A graph over an existing CSR (device buffers, copied): row r's entries are
+ * col[row_ptr[r] .. row_ptr[r+1]).  For the standalone SpMM built by
+ * bgnn_coo_to_csr_dev (SparseCSR, sparse.ts:236-383). */
+BGNN_API int bgnn_graph_create_csr(bgnn_ctx* ctx, const uint32_t* row_ptr, const uint32_t* col,
+                          uint32_t num_rows, uint32_t num_cols, bgnn_graph** out);
+BGNN_API int bgnn_graph_destroy(bgnn_graph* g);
+BGNN_API int bgnn_graph_info(const bgnn_graph* g, uint32_t* num_src, uint32_t* num_dst,
+                    uint64_t* num_edges, int* has_self_loops);
+/* getInDegrees / getOutDegrees (graph.ts:172-195) into device buffers */
+BGNN_API int bgnn_graph_degrees(bgnn_ctx* ctx, const bgnn_graph* g, uint32_t* in_deg, uint32_t* out_deg);
+/* copy the cached CSR out (device buffers; any may be NULL) */
+BGNN_API int bgnn_graph_csr(bgnn_ctx* ctx, const bgnn_graph* g, uint32_t* row_ptr, uint32_t* src_of,
+                   uint32_t* edge_id);
+
+/* ---- fused layer message passing on a graph (device pointers) ---------- */
+/* MessagePassing.gather + scatter{Add,Mean,Max} fused, no [E,F] message
+ * tensor (sparse.ts:400-473): out[N_dst,F] from x[N_src,F]. */
+BGNN_API int bgnn_aggregate(bgnn_ctx* ctx, const bgnn_graph* g, int aggr, const float* x,
+                   uint32_t num_features, float* out);
+/* GCNConv.forward after X*W (gcn.ts:88-156): the self-loop rule (loops
+ * appended only if the graph has none and add_self_loops != 0), symmetric
+ * norm (normalize != 0), edge-order sum, + bias (may be NULL), then act. */
+BGNN_API int bgnn_gcn_propagate(bgnn_ctx* ctx, const bgnn_graph* g, const float* h,
+                       uint32_t num_features, int add_self_loops, int normalize,
+                       const float* bias, int act, double act_param, float* out);
+/* GATConv.forward after X*W (gat.ts:115-254): LeakyReLU edge scores,
+ * exp(s-10) softmax per destination, weighted sum (concat or head mean),
+ * + bias, then act.  h [N, heads*c]; att_src/att_dst [heads, c]. */
+BGNN_API int bgnn_gat(bgnn_ctx* ctx, const bgnn_graph* g, const float* h, uint32_t heads, uint32_t c,
+             const float* att_src, const float* att_dst, double negative_slope, int concat,
+             int add_self_loops, const float* bias, int act, double act_param, float* out);
+/* GINConv step 1-3 (gin.ts:131-157): out = f32((1+eps)*x + sum_j x_j). */
+BGNN_API int bgnn_gin_aggregate(bgnn_ctx* ctx, const bgnn_graph* g, const float* x,
+                       uint32_t num_features, float eps, float* out);
+/* SpMM with per-edge values over the cached CSR (values in CSR order). */
+BGNN_API int bgnn_graph_spmm(bgnn_ctx* ctx, const bgnn_graph* g, const float* values, const float* x,
+                    uint32_t num_features, float* out);
+
+/* ---- dense transforms with fused epilogues ------------------------------ */
+/* out = act(a[m,k] * w[k,n] + bias)   (Tensor.matmul + bias loop + act) */
+BGNN_API int bgnn_linear(bgnn_ctx* ctx, const float* a, const float* w, uint32_t m, uint32_t k,
+                uint32_t n, const float* bias, int act, double act_param, float* out);
+/* SAGEConv steps 3-5 (sage.ts:171-196):
+ * out = act(f32(x*w_self + agg*w_neigh) + bias); w_self may be NULL
+ * (rootWeight = false). */
+BGNN_API int bgnn_sage_linear(bgnn_ctx* ctx, const float* agg, const float* x, const float* w_neigh,
+                     const float* w_self, uint32_t m, uint32_t k, uint32_t n,
+                     const float* bias, int act, double act_param, float* out);
+/* SAGE 'pool' aggregator projection (sage.ts:149-159) applied per node:
+ * out[i,j] = f32(Math.max(0, bias[j] + sum_q x[i,q]*w[q,j])) with a double
+ * accumulator; w is [k, k].  An edge's projected message depends only on its
+ * source node, so max-aggregating these rows equals the reference. */
+BGNN_API int bgnn_pool_projection(bgnn_ctx* ctx, const float* x, const float* w,
+                                  const float* bias, uint32_t m, uint32_t k, float* out);
+/* SAGE L2 normalise (sage.ts:199-214), in place on [m, n]. */
+BGNN_API int bgnn_l2_normalize_rows(bgnn_ctx* ctx, float* x, uint32_t m, uint32_t n);
+/* Global sum pool: g[b,:] = sum over nodes i with batch[i] == b, node order. */
+BGNN_API int bgnn_sum_pool(bgnn_ctx* ctx, const float* x, uint32_t num_nodes, uint32_t num_features,
+                  const uint32_t* batch, uint32_t num_graphs, float* out);
+
+/* ---- partitioning support (node-partitioned multi-GPU) ------------------ */
+/* out[i,:] = x[rows[i],:]  (halo pack; same kernel as gather) */
+BGNN_API int bgnn_pack_rows(bgnn_ctx* ctx, const float* x, uint32_t num_x_rows, const uint32_t* rows,
+                   uint32_t num_rows, uint32_t num_features, float* out);
+
+/* ---- benchmark inputs ------------------------------------------------------ */
+/* Seeded R-MAT edge list [src(E) | dst(E)] on the device (no reference
+ * counterpart: the reference's randomGraph is Erdos-Renyi on Math.random).
+ * Quadrant probabilities a, b, c (d = 1-a-b-c), 2^scale id space, ids >=
+ * num_nodes rejected, optional seeded relabelling of node ids.  Produces the
+ * same list as the numpy generator in browsergnn_b200/synth.py. */
+BGNN_API int bgnn_synth_rmat(bgnn_ctx* ctx, uint64_t seed, int scale, uint32_t num_nodes,
+                             uint64_t num_edges, double a, double b, double c, int permute,
+                             uint32_t* edge_index);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* BGNN_H */

@@ -1,0 +1,118 @@
+/*
+ * bgnn_oracle.h -- CPU restatement of BrowserGNN's message-passing path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This is the oracle that the CUDA library is
+ * checked against; nothing in the product library links, loads or calls it.
+ * Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline / reference
+ * arm may use it.
+ *
+ * Arithmetic model (the reference is TypeScript): every JS local is an IEEE
+ * double, every store into a Float32Array rounds once to float.  The
+ * restatement keeps every local as `double` and casts to `float` exactly
+ * where the reference stores into a Float32Array.  Compile with
+ * -ffp-contract=off and without -ffast-math so no FMA contraction or
+ * reassociation changes the rounding sequence.
+ *
+ * Parity pins: the reference's own known-answer tests (tests/wasm.test.ts,
+ * tests/graph.test.ts) are transcribed as fixtures under tests/golden/ and
+ * checked against these functions.
+ */
+#ifndef BGNN_ORACLE_H
+#define BGNN_ORACLE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- src/backend/wasm/index.ts kernels ---------------------------------- */
+void orc_matmul(const float* a, const float* b, int64_t m, int64_t k, int64_t n, float* out);
+void orc_scatter_add(const float* src, const uint32_t* index, int64_t num_msgs,
+                     int64_t num_nodes, int64_t num_features, float* out);
+void orc_scatter_mean(const float* src, const uint32_t* index, int64_t num_msgs,
+                      int64_t num_nodes, int64_t num_features, float* out);
+void orc_scatter_max(const float* src, const uint32_t* index, int64_t num_msgs,
+                     int64_t num_nodes, int64_t num_features, float* out);
+void orc_gather(const float* src, const uint32_t* index, int64_t num_idx,
+                int64_t num_features, float* out);
+void orc_relu(const float* x, int64_t n, float* out);
+void orc_add(const float* a, const float* b, int64_t n, float* out);
+void orc_spmv(const uint32_t* row_ptr, const uint32_t* col, const float* val,
+              const float* x, int64_t num_rows, float* out);
+void orc_spmm(const uint32_t* row_ptr, const uint32_t* col, const float* val,
+              const float* dense, int64_t num_rows, int64_t num_features, float* out);
+
+/* ---- src/core/sparse.ts ------------------------------------------------- */
+void orc_coo_spmm(const uint32_t* rows, const uint32_t* cols, const float* vals,
+                  int64_t nnz, int64_t m, const float* dense, int64_t k, float* out);
+/* SparseCSR.fromCOO: stable sort by (row, col); returns 0 or -1 on OOM. */
+int orc_coo_to_csr(const uint32_t* rows, const uint32_t* cols, const float* vals,
+                   int64_t nnz, int64_t num_rows, uint32_t* row_ptr,
+                   uint32_t* col_out, float* val_out);
+void orc_gcn_norm(const uint32_t* edge_index, int64_t num_edges, int64_t num_nodes,
+                  int add_self_loops, float* out);
+
+/* ---- src/core/graph.ts -------------------------------------------------- */
+/* returns -1 if valid, else the position of the first out-of-range index */
+int64_t orc_validate_edges(const uint32_t* edge_index, int64_t num_edges, int64_t num_nodes);
+void orc_in_degree(const uint32_t* edge_index, int64_t num_edges, int64_t num_nodes, uint32_t* out);
+void orc_out_degree(const uint32_t* edge_index, int64_t num_edges, int64_t num_nodes, uint32_t* out);
+int orc_has_self_loops(const uint32_t* edge_index, int64_t num_edges);
+/* out has room for 2*(num_edges+num_nodes); returns the new edge count */
+int64_t orc_add_self_loops(const uint32_t* edge_index, int64_t num_edges, int64_t num_nodes,
+                           uint32_t* out);
+
+/* ---- activations (src/core/tensor.ts, src/nn/activation.ts, gin.ts) ---- */
+void orc_elu(const float* x, int64_t n, double alpha, float* out);
+void orc_leaky_relu(const float* x, int64_t n, double slope, float* out);
+void orc_relu_max(const float* x, int64_t n, float* out); /* Math.max(0, x) */
+
+/* ---- layer forwards (src/layers/{gcn,gat,sage,gin}.ts), reference data layout ----------- */
+/* weight [fin, fout]; bias may be NULL.  add_self_loops / normalize follow
+ * GCNConvConfig.  out [N, fout]. */
+int orc_gcn_forward(const float* x, int64_t n, int64_t fin, const uint32_t* edge_index,
+                    int64_t num_edges, const float* weight, const float* bias, int64_t fout,
+                    int add_self_loops, int normalize, float* out);
+/* weight [fin, heads*c]; att_src/att_dst [heads, c]; bias [heads*c or c] or NULL */
+int orc_gat_forward(const float* x, int64_t n, int64_t fin, const uint32_t* edge_index,
+                    int64_t num_edges, const float* weight, const float* att_src,
+                    const float* att_dst, const float* bias, int64_t heads, int64_t c,
+                    double negative_slope, int concat, int add_self_loops, float* out);
+/* aggr: 0 mean, 1 max, 2 sum, 3 pool.  lin_self NULL => rootWeight=false. */
+int orc_sage_forward(const float* x, int64_t n, int64_t fin, const uint32_t* edge_index,
+                     int64_t num_edges, int aggr, const float* lin_neighbor,
+                     const float* lin_self, const float* bias, const float* pool_weight,
+                     const float* pool_bias, int64_t fout, int normalize, float* out);
+int orc_gin_forward(const float* x, int64_t n, int64_t fin, const uint32_t* edge_index,
+                    int64_t num_edges, float eps, const float* w1, const float* b1,
+                    int64_t hidden, const float* w2, const float* b2, int64_t fout,
+                    float* out);
+/* global sum pool over a batch vector (nodes visited in node order) */
+void orc_sum_pool(const float* x, int64_t n, int64_t f, const uint32_t* batch,
+                  int64_t num_graphs, float* out);
+
+/* ---- streamed / row-parallel restatement (same per-row order) ---------- */
+/* Destination-keyed CSR with each row's edges in COO order (stable counting
+ * sort).  row_ptr [N+1], src_of [E] (source node), eid [E] (edge id). */
+int orc_dst_csr(const uint32_t* edge_index, int64_t num_edges, int64_t num_nodes,
+                uint32_t* row_ptr, uint32_t* src_of, uint32_t* eid);
+/* op: 0 sum, 1 mean, 2 max, 3 gcn (norm from in-degree of the given graph),
+ * self_loop_tail: treat every row as having one extra edge (i -> i) after its
+ * own edges (the GCN/GAT self-loop insertion).  threads <= 0: all cores. */
+void orc_csr_aggregate(const uint32_t* row_ptr, const uint32_t* src_of, int64_t num_rows,
+                       const float* x, int64_t f, int op, int self_loop_tail,
+                       int threads, float* out);
+/* SAGE layer forward over a destination CSR, row-parallel, same bits as
+ * orc_sage_forward (mean/max/sum aggregators). */
+int orc_sage_forward_csr(const uint32_t* row_ptr, const uint32_t* src_of, int64_t n,
+                         const float* x, int64_t fin, int aggr, const float* lin_neighbor,
+                         const float* lin_self, const float* bias, int64_t fout,
+                         int relu, int threads, float* out);
+void orc_matmul_par(const float* a, const float* b, int64_t m, int64_t k, int64_t n,
+                    int threads, float* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,335 @@
+"""ctypes front end for the CPU oracle (libbgnn_oracle.so).
+
+TEST INFRASTRUCTURE ONLY: the restatement of BrowserGNN's CPU message-passing
+path that the CUDA library is checked against.  Only tests/,
+``__graft_entry__.smoke()`` and bench.py's CPU-baseline / reference arm import
+this module; the product package never does.
+
+Every function takes and returns numpy arrays (float32 features, uint32
+indices) and calls the C restatement in ``bgnn_oracle.c``, which cites the
+reference function it follows.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "libbgnn_oracle.so")
+_lib = None
+
+_F = ctypes.POINTER(ctypes.c_float)
+_U = ctypes.POINTER(ctypes.c_uint32)
+_I64 = ctypes.c_int64
+
+
+def build() -> str:
+    """Compile the oracle with its Makefile (gcc, -ffp-contract=off)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        _lib = ctypes.CDLL(_LIB_PATH)
+        _declare(_lib)
+    return _lib
+
+
+def _declare(L):
+    v = None
+    sig = {
+        "orc_matmul": (v, [_F, _F, _I64, _I64, _I64, _F]),
+        "orc_matmul_par": (v, [_F, _F, _I64, _I64, _I64, ctypes.c_int, _F]),
+        "orc_scatter_add": (v, [_F, _U, _I64, _I64, _I64, _F]),
+        "orc_scatter_mean": (v, [_F, _U, _I64, _I64, _I64, _F]),
+        "orc_scatter_max": (v, [_F, _U, _I64, _I64, _I64, _F]),
+        "orc_gather": (v, [_F, _U, _I64, _I64, _F]),
+        "orc_relu": (v, [_F, _I64, _F]),
+        "orc_add": (v, [_F, _F, _I64, _F]),
+        "orc_spmv": (v, [_U, _U, _F, _F, _I64, _F]),
+        "orc_spmm": (v, [_U, _U, _F, _F, _I64, _I64, _F]),
+        "orc_coo_spmm": (v, [_U, _U, _F, _I64, _I64, _F, _I64, _F]),
+        "orc_coo_to_csr": (ctypes.c_int, [_U, _U, _F, _I64, _I64, _U, _U, _F]),
+        "orc_gcn_norm": (v, [_U, _I64, _I64, ctypes.c_int, _F]),
+        "orc_validate_edges": (_I64, [_U, _I64, _I64]),
+        "orc_in_degree": (v, [_U, _I64, _I64, _U]),
+        "orc_out_degree": (v, [_U, _I64, _I64, _U]),
+        "orc_has_self_loops": (ctypes.c_int, [_U, _I64]),
+        "orc_add_self_loops": (_I64, [_U, _I64, _I64, _U]),
+        "orc_elu": (v, [_F, _I64, ctypes.c_double, _F]),
+        "orc_leaky_relu": (v, [_F, _I64, ctypes.c_double, _F]),
+        "orc_relu_max": (v, [_F, _I64, _F]),
+        "orc_gcn_forward": (ctypes.c_int, [_F, _I64, _I64, _U, _I64, _F, _F, _I64,
+                                           ctypes.c_int, ctypes.c_int, _F]),
+        "orc_gat_forward": (ctypes.c_int, [_F, _I64, _I64, _U, _I64, _F, _F, _F, _F, _I64,
+                                           _I64, ctypes.c_double, ctypes.c_int, ctypes.c_int,
+                                           _F]),
+        "orc_sage_forward": (ctypes.c_int, [_F, _I64, _I64, _U, _I64, ctypes.c_int, _F, _F, _F,
+                                            _F, _F, _I64, ctypes.c_int, _F]),
+        "orc_gin_forward": (ctypes.c_int, [_F, _I64, _I64, _U, _I64, ctypes.c_float, _F, _F,
+                                           _I64, _F, _F, _I64, _F]),
+        "orc_sum_pool": (v, [_F, _I64, _I64, _U, _I64, _F]),
+        "orc_dst_csr": (ctypes.c_int, [_U, _I64, _I64, _U, _U, _U]),
+        "orc_csr_aggregate": (v, [_U, _U, _I64, _F, _I64, ctypes.c_int, ctypes.c_int,
+                                  ctypes.c_int, _F]),
+        "orc_sage_forward_csr": (ctypes.c_int, [_U, _U, _I64, _F, _I64, ctypes.c_int, _F, _F,
+                                                _F, _I64, ctypes.c_int, ctypes.c_int, _F]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+
+
+def _f(a):
+    if a is None:
+        return None
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    return a
+
+
+def _u(a):
+    return np.ascontiguousarray(a, dtype=np.uint32)
+
+
+def _pf(a):
+    return None if a is None else a.ctypes.data_as(_F)
+
+
+def _pu(a):
+    return None if a is None else a.ctypes.data_as(_U)
+
+
+# ---- src/backend/wasm/index.ts ---------------------------------------------
+def matmul(a, b, m, k, n, threads=1):
+    a, b = _f(a), _f(b)
+    out = np.empty(m * n, np.float32)
+    if threads == 1:
+        lib().orc_matmul(_pf(a), _pf(b), m, k, n, _pf(out))
+    else:
+        lib().orc_matmul_par(_pf(a), _pf(b), m, k, n, threads, _pf(out))
+    return out
+
+
+def _scatter(name, src, index, num_nodes, nf):
+    src, index = _f(src), _u(index)
+    out = np.empty(num_nodes * nf, np.float32)
+    getattr(lib(), name)(_pf(src), _pu(index), index.size, num_nodes, nf, _pf(out))
+    return out
+
+
+def scatter_add(src, index, num_nodes, nf):
+    return _scatter("orc_scatter_add", src, index, num_nodes, nf)
+
+
+def scatter_mean(src, index, num_nodes, nf):
+    return _scatter("orc_scatter_mean", src, index, num_nodes, nf)
+
+
+def scatter_max(src, index, num_nodes, nf):
+    return _scatter("orc_scatter_max", src, index, num_nodes, nf)
+
+
+def gather(src, index, nf):
+    src, index = _f(src), _u(index)
+    out = np.empty(index.size * nf, np.float32)
+    lib().orc_gather(_pf(src), _pu(index), index.size, nf, _pf(out))
+    return out
+
+
+def relu(x):
+    x = _f(x)
+    out = np.empty_like(x)
+    lib().orc_relu(_pf(x), x.size, _pf(out))
+    return out
+
+
+def relu_max(x):
+    x = _f(x)
+    out = np.empty_like(x)
+    lib().orc_relu_max(_pf(x), x.size, _pf(out))
+    return out
+
+
+def elu(x, alpha=1.0):
+    x = _f(x)
+    out = np.empty_like(x)
+    lib().orc_elu(_pf(x), x.size, alpha, _pf(out))
+    return out
+
+
+def leaky_relu(x, slope=0.01):
+    x = _f(x)
+    out = np.empty_like(x)
+    lib().orc_leaky_relu(_pf(x), x.size, slope, _pf(out))
+    return out
+
+
+def add(a, b):
+    a, b = _f(a), _f(b)
+    out = np.empty_like(a)
+    lib().orc_add(_pf(a), _pf(b), a.size, _pf(out))
+    return out
+
+
+def spmv(row_ptr, col, val, x, num_rows):
+    row_ptr, col, val, x = _u(row_ptr), _u(col), _f(val), _f(x)
+    out = np.empty(num_rows, np.float32)
+    lib().orc_spmv(_pu(row_ptr), _pu(col), _pf(val), _pf(x), num_rows, _pf(out))
+    return out
+
+
+def spmm(row_ptr, col, val, dense, num_rows, nf):
+    row_ptr, col, val, dense = _u(row_ptr), _u(col), _f(val), _f(dense)
+    out = np.empty(num_rows * nf, np.float32)
+    lib().orc_spmm(_pu(row_ptr), _pu(col), _pf(val), _pf(dense), num_rows, nf, _pf(out))
+    return out
+
+
+def coo_spmm(rows, cols, vals, m, dense, k):
+    rows, cols, vals, dense = _u(rows), _u(cols), _f(vals), _f(dense)
+    out = np.empty(m * k, np.float32)
+    lib().orc_coo_spmm(_pu(rows), _pu(cols), _pf(vals), rows.size, m, _pf(dense), k, _pf(out))
+    return out
+
+
+# ---- src/core/sparse.ts / graph.ts ------------------------------------------
+def coo_to_csr(rows, cols, vals, num_rows):
+    rows, cols = _u(rows), _u(cols)
+    vals = None if vals is None else _f(vals)
+    nnz = rows.size
+    row_ptr = np.empty(num_rows + 1, np.uint32)
+    col_out = np.empty(max(nnz, 1), np.uint32)
+    val_out = np.empty(max(nnz, 1), np.float32)
+    rc = lib().orc_coo_to_csr(_pu(rows), _pu(cols), _pf(vals), nnz, num_rows, _pu(row_ptr),
+                              _pu(col_out), _pf(val_out))
+    if rc != 0:
+        raise ValueError(f"orc_coo_to_csr failed ({rc})")
+    return row_ptr, col_out[:nnz], val_out[:nnz]
+
+
+def gcn_norm(edge_index, num_edges, num_nodes, add_self_loops=True):
+    ei = _u(edge_index)
+    out = np.empty(num_edges, np.float32)
+    lib().orc_gcn_norm(_pu(ei), num_edges, num_nodes, int(add_self_loops), _pf(out))
+    return out
+
+
+def validate_edges(edge_index, num_edges, num_nodes):
+    ei = _u(edge_index)
+    return int(lib().orc_validate_edges(_pu(ei), num_edges, num_nodes))
+
+
+def in_degree(edge_index, num_edges, num_nodes):
+    ei = _u(edge_index)
+    out = np.empty(num_nodes, np.uint32)
+    lib().orc_in_degree(_pu(ei), num_edges, num_nodes, _pu(out))
+    return out
+
+
+def out_degree(edge_index, num_edges, num_nodes):
+    ei = _u(edge_index)
+    out = np.empty(num_nodes, np.uint32)
+    lib().orc_out_degree(_pu(ei), num_edges, num_nodes, _pu(out))
+    return out
+
+
+def has_self_loops(edge_index, num_edges):
+    return bool(lib().orc_has_self_loops(_pu(_u(edge_index)), num_edges))
+
+
+def add_self_loops(edge_index, num_edges, num_nodes):
+    ei = _u(edge_index)
+    out = np.empty(2 * (num_edges + num_nodes), np.uint32)
+    ne = int(lib().orc_add_self_loops(_pu(ei), num_edges, num_nodes, _pu(out)))
+    return out[:2 * ne], ne
+
+
+# ---- layer forwards (src/layers) ---------------------------------------------
+def gcn_forward(x, n, fin, edge_index, num_edges, weight, bias, fout, add_self_loops=True,
+                normalize=True):
+    out = np.empty(n * fout, np.float32)
+    rc = lib().orc_gcn_forward(_pf(_f(x)), n, fin, _pu(_u(edge_index)), num_edges,
+                               _pf(_f(weight)), _pf(_f(bias)), fout, int(add_self_loops),
+                               int(normalize), _pf(out))
+    assert rc == 0
+    return out
+
+
+def gat_forward(x, n, fin, edge_index, num_edges, weight, att_src, att_dst, bias, heads, c,
+                negative_slope=0.2, concat=True, add_self_loops=True):
+    od = heads * c if concat else c
+    out = np.empty(n * od, np.float32)
+    rc = lib().orc_gat_forward(_pf(_f(x)), n, fin, _pu(_u(edge_index)), num_edges,
+                               _pf(_f(weight)), _pf(_f(att_src)), _pf(_f(att_dst)),
+                               _pf(_f(bias)), heads, c, float(negative_slope), int(concat),
+                               int(add_self_loops), _pf(out))
+    assert rc == 0
+    return out
+
+
+SAGE_AGGR = {"mean": 0, "max": 1, "sum": 2, "pool": 3}
+
+
+def sage_forward(x, n, fin, edge_index, num_edges, aggr, lin_neighbor, lin_self, bias, fout,
+                 normalize=False, pool_weight=None, pool_bias=None):
+    out = np.empty(n * fout, np.float32)
+    rc = lib().orc_sage_forward(_pf(_f(x)), n, fin, _pu(_u(edge_index)), num_edges,
+                                SAGE_AGGR[aggr], _pf(_f(lin_neighbor)), _pf(_f(lin_self)),
+                                _pf(_f(bias)), _pf(_f(pool_weight)), _pf(_f(pool_bias)), fout,
+                                int(normalize), _pf(out))
+    assert rc == 0
+    return out
+
+
+def gin_forward(x, n, fin, edge_index, num_edges, eps, w1, b1, hidden, w2, b2, fout):
+    out = np.empty(n * fout, np.float32)
+    rc = lib().orc_gin_forward(_pf(_f(x)), n, fin, _pu(_u(edge_index)), num_edges,
+                               float(eps), _pf(_f(w1)), _pf(_f(b1)), hidden, _pf(_f(w2)),
+                               _pf(_f(b2)), fout, _pf(out))
+    assert rc == 0
+    return out
+
+
+def sum_pool(x, n, f, batch, num_graphs):
+    out = np.empty(num_graphs * f, np.float32)
+    lib().orc_sum_pool(_pf(_f(x)), n, f, _pu(_u(batch)), num_graphs, _pf(out))
+    return out
+
+
+# ---- streamed / row-parallel -------------------------------------------------
+def dst_csr(edge_index, num_edges, num_nodes):
+    ei = _u(edge_index)
+    row_ptr = np.empty(num_nodes + 1, np.uint32)
+    src_of = np.empty(max(num_edges, 1), np.uint32)
+    eid = np.empty(max(num_edges, 1), np.uint32)
+    rc = lib().orc_dst_csr(_pu(ei), num_edges, num_nodes, _pu(row_ptr), _pu(src_of), _pu(eid))
+    assert rc == 0
+    return row_ptr, src_of[:num_edges], eid[:num_edges]
+
+
+AGG_OPS = {"sum": 0, "mean": 1, "max": 2, "gcn": 3}
+
+
+def csr_aggregate(row_ptr, src_of, num_rows, x, f, op, self_loop_tail=False, threads=0):
+    out = np.empty(num_rows * f, np.float32)
+    lib().orc_csr_aggregate(_pu(_u(row_ptr)), _pu(_u(src_of)), num_rows, _pf(_f(x)), f,
+                            AGG_OPS[op], int(self_loop_tail), threads, _pf(out))
+    return out
+
+
+def sage_forward_csr(row_ptr, src_of, n, x, fin, aggr, lin_neighbor, lin_self, bias, fout,
+                     relu=False, threads=0):
+    out = np.empty(n * fout, np.float32)
+    rc = lib().orc_sage_forward_csr(_pu(_u(row_ptr)), _pu(_u(src_of)), n, _pf(_f(x)), fin,
+                                    SAGE_AGGR[aggr], _pf(_f(lin_neighbor)), _pf(_f(lin_self)),
+                                    _pf(_f(bias)), fout, int(relu), threads, _pf(out))
+    assert rc == 0
+    return out

@@ -1,0 +1,106 @@
+"""Pin the CPU oracle to the reference's own known-answer tests.
+
+The vectors in tests/golden/reference_kats.json are transcribed from the
+reference's vitest files (tests/wasm.test.ts, tests/graph.test.ts); each case
+names its source lines.  These run on the CPU only.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as orc
+
+GOLD = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "reference_kats.json")))
+
+
+def close(got, want, case):
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    assert got.shape == want.shape, case["src"]
+    if case.get("exact"):
+        assert np.array_equal(got, want), case["src"]
+    else:
+        # vitest toBeCloseTo(x, d): |got - want| < 10^-d / 2
+        assert np.all(np.abs(got - want) < 10.0 ** (-case["tol_digits"]) / 2), case["src"]
+
+
+@pytest.mark.parametrize("case", GOLD["matmul"], ids=lambda c: c["src"])
+def test_matmul(case):
+    close(orc.matmul(case["a"], case["b"], case["m"], case["k"], case["n"]), case["expect"], case)
+
+
+@pytest.mark.parametrize("op", ["scatter_add", "scatter_mean", "scatter_max"])
+def test_scatter(op):
+    for case in GOLD[op]:
+        got = getattr(orc, op)(case["x"], case["index"], case["num_nodes"], case["num_features"])
+        close(got, case["expect"], case)
+
+
+def test_gather():
+    for case in GOLD["gather"]:
+        close(orc.gather(case["x"], case["index"], case["num_features"]), case["expect"], case)
+
+
+def test_relu_add():
+    for case in GOLD["relu"]:
+        close(orc.relu(case["x"]), case["expect"], case)
+    for case in GOLD["add"]:
+        close(orc.add(case["a"], case["b"]), case["expect"], case)
+
+
+def test_spmv_spmm():
+    for case in GOLD["spmv"]:
+        close(orc.spmv(case["row_ptr"], case["col"], case["val"], case["x"], case["num_rows"]),
+              case["expect"], case)
+    for case in GOLD["spmm"]:
+        got = orc.spmm(case["row_ptr"], case["col"], case["val"], case["dense"], case["num_rows"],
+                       case["num_features"])
+        close(got, case["expect"], case)
+
+
+def test_degrees():
+    for case in GOLD["degrees"]:
+        ei = case["edge_index"]
+        assert list(orc.in_degree(ei, case["num_edges"], case["num_nodes"])) == case["in_degree"]
+        assert list(orc.out_degree(ei, case["num_edges"], case["num_nodes"])) == case["out_degree"]
+
+
+def test_validate():
+    for case in GOLD["validate"]:
+        bad = orc.validate_edges(case["edge_index"], case["num_edges"], case["num_nodes"])
+        assert (bad < 0) == case["valid"], case["src"]
+
+
+def test_self_loops():
+    for case in GOLD["self_loops"]:
+        ei, e, n = case["edge_index"], case["num_edges"], case["num_nodes"]
+        assert orc.has_self_loops(ei, e) == case["has_self_loops"]
+        if "after_add_num_edges" in case:
+            new_ei, ne = orc.add_self_loops(ei, e, n)
+            assert ne == case["after_add_num_edges"]
+            assert orc.has_self_loops(new_ei, ne) == case["after_add_has_self_loops"]
+            # original edges first, loops appended in node order (graph.ts:246-258)
+            assert list(new_ei[:e]) == ei[:e] and list(new_ei[ne:ne + e]) == ei[e:]
+            assert list(new_ei[e:ne]) == list(range(n)) == list(new_ei[ne + e:])
+
+
+def test_gcn_norm_hand_case():
+    # Unpinned by the reference's tests; checked by hand: path 0->1->2 plus
+    # self-loop counts (deg = [1, 2, 2] with addSelfLoops=True).
+    ei = [0, 1, 1, 2]
+    w = orc.gcn_norm(ei, 2, 3, True)
+    want = np.array([1 / np.sqrt(1) * 1 / np.sqrt(2), 1 / np.sqrt(2) * 1 / np.sqrt(2)])
+    assert np.allclose(w, want.astype(np.float32), rtol=0, atol=1e-7)
+
+
+def test_coo_to_csr_stable_sort():
+    # fromCOO sorts by (row, col) and keeps ties (duplicate edges) in input order.
+    rows = [2, 0, 2, 0, 1, 2]
+    cols = [1, 3, 0, 3, 2, 1]
+    vals = [10, 20, 30, 40, 50, 60]
+    rp, ci, va = orc.coo_to_csr(rows, cols, vals, 4)
+    assert list(rp) == [0, 2, 3, 6, 6]
+    assert list(ci) == [3, 3, 2, 0, 1, 1]
+    assert list(va) == [20, 40, 50, 30, 10, 60]
