@@ -1,0 +1,562 @@
+"""Benchmark: aggregated edges/s per layer forward on B200.
+
+Workload (one step): a full-graph forward of the 3-layer GraphSAGE-mean stack
+(100 -> 256 -> 256 -> 47, root weight, ReLU between layers) over a seeded
+R-MAT graph with 2,450,000 nodes and 62,000,000 directed edges (a=0.57,
+b=c=0.19, ids permuted) and N(0,1) features.  Metric = edges aggregated per
+second per layer forward = 3 * E / step time.  Inputs are resident in HBM
+(features 0.98-2.5 GB per layer, far larger than the 126 MB L2, so no L2
+flush is needed between steps).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+N > 1 (torchrun, one rank per GPU): the graph's destination rows are
+partitioned by edge count across ranks; each layer exchanges the halo rows
+with NCCL all-to-all before the local aggregation (strong scaling).
+
+Extra keys: roofline of the dominant kernel (the F=256 aggregation), the CPU
+baseline (the oracle on a 1/64 sample of the workload, all host threads),
+e2e through the public API with host buffers, clocks during the timed region,
+and at N=1 the standalone SpMM sweep (scale-24 R-MAT, 2^28 edges).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "aggregated edges/s per layer forward"
+UNIT = "edges/s"
+WIDTHS = [100, 256, 256, 47]
+FALLBACK_HBM_GBS = 6650.0
+
+
+def env_int(name, default):
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        try:
+            d = json.load(open(p))
+            return float(d["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def profile_traffic(name):
+    """dram bytes per launch from a committed ncu summary (profiles/<name>.md,
+    a line 'dram_bytes_per_launch: <int>'), or None."""
+    p = os.path.join(ROOT, "profiles", name + ".md")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.strip().startswith("dram_bytes_per_launch:"):
+            try:
+                return int(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        os.unlink(self.path)
+        loaded = [s for s in sm if smax and s > 0.5 * smax] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": smax,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------------------
+# the SAGE stack on libbgnn_cuda
+# ---------------------------------------------------------------------------
+def make_weights(seed):
+    from browsergnn_b200 import synth
+
+    rng = np.random.default_rng(seed)
+    layers = []
+    for fin, fout in zip(WIDTHS[:-1], WIDTHS[1:]):
+        layers.append({"lin_neighbor": synth.glorot(fin, fout, rng),
+                       "lin_self": synth.glorot(fin, fout, rng),
+                       "bias": rng.uniform(-0.1, 0.1, fout).astype(np.float32)})
+    return layers
+
+
+def build_layers(weights, device):
+    import browsergnn_b200 as bg
+
+    layers = []
+    for (fin, fout), w in zip(zip(WIDTHS[:-1], WIDTHS[1:]), weights):
+        lay = bg.SAGEConv(inChannels=fin, outChannels=fout, aggregator="mean")
+        lay.loadStateDict(w)
+        lay.to_device(device)
+        layers.append(lay)
+    return layers
+
+
+def sage_forward(layers, dg, x, exchange=None, timers=None):
+    """Three SAGEConv layers (aggregate -> fused dual GEMM + bias + ReLU).
+    `exchange(x_local) -> x_ext` fills halo rows for a partitioned graph.
+    `timers` collects CUDA events around each aggregation launch."""
+    import torch
+
+    from browsergnn_b200.backend import ptr
+
+    ctx = dg.ctx
+    n_own = dg.num_dst
+    h = x
+    for li, lay in enumerate(layers):
+        fin, fout = lay.inChannels, lay.outChannels
+        src = exchange(h) if exchange is not None else h
+        agg = torch.empty((n_own, fin), dtype=torch.float32, device=h.device)
+        if timers is not None:
+            ev0 = torch.cuda.Event(enable_timing=True)
+            ev1 = torch.cuda.Event(enable_timing=True)
+            ev0.record()
+        ctx.call("bgnn_aggregate", dg.h, 1, ptr(src), fin, ptr(agg))
+        if timers is not None:
+            ev1.record()
+            timers.append((li, fin, ev0, ev1))
+        out = torch.empty((n_own, fout), dtype=torch.float32, device=h.device)
+        act = 1 if li < len(layers) - 1 else 0  # ReLU between layers (wasmRelu)
+        ctx.call("bgnn_sage_linear", ptr(agg), ptr(h), ptr(lay.p("lin_neighbor")),
+                 ptr(lay.p("lin_self")), n_own, fin, fout, ptr(lay.p("bias")), act, 0.0,
+                 ptr(out))
+        h = out
+    return h
+
+
+# ---------------------------------------------------------------------------
+# partitioning (N > 1)
+# ---------------------------------------------------------------------------
+class Partition:
+    """Destination-row partition of the graph with a halo plan (built once)."""
+
+    def __init__(self, ei, n, e, rank, world, device):
+        import torch
+        import torch.distributed as dist
+
+        from browsergnn_b200.graph import DeviceGraph
+
+        src = ei[:e].long()
+        dst = ei[e:].long()
+        src[src < 0] += 1 << 32
+        dst[dst < 0] += 1 << 32
+        indeg = torch.bincount(dst, minlength=n)
+        cum = torch.cumsum(indeg, 0)
+        # contiguous row ranges with ~E/world edges each
+        targets = torch.arange(1, world, device=cum.device) * (e / world)
+        cuts = torch.searchsorted(cum.double(), targets.double()).tolist()
+        bounds = [0] + [int(c) + 1 for c in cuts] + [n]
+        for i in range(1, len(bounds)):
+            bounds[i] = max(bounds[i], bounds[i - 1])
+        self.bounds = bounds
+        lo, hi = bounds[rank], bounds[rank + 1]
+        self.lo, self.hi, self.n_own = lo, hi, hi - lo
+        keep = (dst >= lo) & (dst < hi)  # COO order preserved: stable per row
+        ls, ld = src[keep], dst[keep] - lo
+        own = (ls >= lo) & (ls < hi)
+        halo = torch.unique(ls[~own])  # sorted global ids
+        self.n_halo = int(halo.numel())
+        col = torch.empty_like(ls)
+        col[own] = ls[own] - lo
+        col[~own] = self.n_own + torch.searchsorted(halo, ls[~own])
+        self.e_local = int(ls.numel())
+        local_ei = torch.cat([col, ld]).to(torch.int64)
+        local_ei = torch.where(local_ei >= (1 << 31), local_ei - (1 << 32), local_ei).to(torch.int32)
+        self.graph = DeviceGraph(local_ei, self.e_local, self.n_own + self.n_halo, self.n_own,
+                                 device=device)
+        # requests: halo ids grouped by owner (ranges are increasing, halo sorted)
+        owner = torch.searchsorted(torch.tensor(bounds[1:], device=halo.device), halo, right=True)
+        send_req = torch.bincount(owner, minlength=world).to(torch.int64)
+        recv_req = torch.empty_like(send_req)
+        dist.all_to_all_single(recv_req, send_req)
+        self.recv_splits = send_req.tolist()   # rows I receive from each rank
+        self.send_splits = recv_req.tolist()   # rows I send to each rank
+        req_ids = torch.empty(sum(self.send_splits), dtype=torch.int64, device=halo.device)
+        dist.all_to_all_single(req_ids, halo.to(torch.int64), self.send_splits, self.recv_splits)
+        self.send_rows = (req_ids - lo).to(torch.int32).contiguous()
+        self.n_send = int(self.send_rows.numel())
+        self.x_local = None
+
+    def exchange_fn(self, ctx):
+        import torch
+        import torch.distributed as dist
+
+        from browsergnn_b200.backend import ptr
+
+        def exchange(h):
+            f = h.shape[1]
+            ext = torch.empty((self.n_own + self.n_halo, f), dtype=torch.float32, device=h.device)
+            ext[: self.n_own].copy_(h)
+            send = torch.empty((self.n_send, f), dtype=torch.float32, device=h.device)
+            if self.n_send:
+                ctx.call("bgnn_pack_rows", ptr(h), self.n_own, ptr(self.send_rows), self.n_send, f,
+                         ptr(send))
+            recv = ext[self.n_own:]
+            dist.all_to_all_single(recv, send, self.recv_splits, self.send_splits)
+            return ext
+
+        return exchange
+
+
+# ---------------------------------------------------------------------------
+# SpMM sweep (standalone CSR SpMM, scale-24 R-MAT, 2^28 edges)
+# ---------------------------------------------------------------------------
+def spmm_sweep(steps, warmup, hbm_peak):
+    import torch
+
+    import browsergnn_b200 as bg
+    from browsergnn_b200 import synth
+    from browsergnn_b200.backend import ptr
+
+    n, e, scale = 1 << synth.SPMM_SCALE, synth.SPMM_E, synth.SPMM_SCALE
+    seed = synth.seed_for(5)
+    ei = synth.rmat_edges_gpu(scale, n, e, seed)
+    ctx = bg.get_context()
+    # values f32(u * dinv[src] * dinv[dst]) with u ~ U(0,1] and dinv from the in-degree
+    dinv = bg.compute_gcn_norm(ei, e, n, False)  # dinv[s]*dinv[t] per edge
+    u = 1.0 - torch.rand(e, device="cuda", generator=torch.Generator("cuda").manual_seed(seed))
+    vals = (u.float() * dinv).contiguous()
+    del dinv
+    rows = ei[:e]
+    cols = ei[e:]
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    csr = bg.SparseCSR.fromCOO(bg.SparseCOO(rows, cols, vals, (n, n)))
+    t1.record()
+    torch.cuda.synchronize()
+    build_ms = t0.elapsed_time(t1)
+    del ei, rows, cols, vals, u
+    g = csr.graph()
+    res = {"workload": f"spmm-rmat-s{scale}-{n}n-{e}e", "csr_build_ms": round(build_ms, 3)}
+    per_f = {}
+    gen = torch.Generator("cuda").manual_seed(seed + 1)
+    for f in (32, 64, 128, 256):
+        x = torch.randn((n, f), device="cuda", generator=gen)
+        out = torch.empty((n, f), device="cuda")
+        for _ in range(warmup):
+            ctx.call("bgnn_graph_spmm", g.h, ptr(csr.values), ptr(x), f, ptr(out))
+        torch.cuda.synchronize()
+        evs = []
+        for _ in range(steps):
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            ctx.call("bgnn_graph_spmm", g.h, ptr(csr.values), ptr(x), f, ptr(out))
+            b.record()
+            evs.append((a, b))
+        torch.cuda.synchronize()
+        ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+        bytes_alg = 4 * (n + 1) + 8 * e + 4 * f * e + 4 * f * n  # rowPtr, col, val, gathers, out
+        gbs = bytes_alg / (ms * 1e-3) / 1e9
+        per_f[str(f)] = {"ms": round(ms, 3), "edges_per_s": e / (ms * 1e-3),
+                         "gather_model_GBps": round(gbs, 1),
+                         "hbm_frac_gather_model": round(gbs / hbm_peak, 3),
+                         "compulsory_GBps": round((4 * (n + 1) + 8 * e + 8 * f * n)
+                                                  / (ms * 1e-3) / 1e9, 1)}
+        del x, out
+    res["per_feature_width"] = per_f
+    g.close()
+    return res
+
+
+# ---------------------------------------------------------------------------
+# CPU legs: the oracle restatement of the reference CPU path
+# ---------------------------------------------------------------------------
+def cpu_sample_forward(threads, frac=64, repeats=1):
+    """3-layer SAGE forward of the oracle on a 1/frac sample of the workload
+    (same degree distribution, widths and weights).  Returns (edges/s, desc)."""
+    sys.path.insert(0, ROOT)
+    from browsergnn_b200 import synth
+    from oracle import oracle as orc
+
+    w = synth.sage_rmat_small(frac)
+    weights = make_weights(synth.seed_for(4))
+    rp, so, _ = orc.dst_csr(w.edge_index, w.num_edges, w.num_nodes)
+    times = []
+    for _ in range(repeats):
+        h = w.x
+        t0 = time.perf_counter()
+        for li, (fin, fout) in enumerate(zip(WIDTHS[:-1], WIDTHS[1:])):
+            lw = weights[li]
+            h = orc.sage_forward_csr(rp, so, w.num_nodes, h, fin, "mean", lw["lin_neighbor"],
+                                     lw["lin_self"], lw["bias"], fout, relu=li < 2,
+                                     threads=threads)
+        times.append(time.perf_counter() - t0)
+    t = min(times)
+    desc = (f"3-layer SAGE-mean forward of the CPU restatement on a 1/{frac} sample of the "
+            f"workload: R-MAT {w.num_nodes} nodes / {w.num_edges} edges, same widths")
+    return 3 * w.num_edges / t, desc, w.num_edges, t
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    from oracle import oracle as orc
+
+    orc.lib()
+    threads = os.cpu_count() or 1
+    # each step: the sample forward on all host threads
+    for _ in range(args.warmup):
+        cpu_sample_forward(threads, repeats=1)
+    vals, secs = [], []
+    for _ in range(args.steps):
+        v, desc, e_s, t = cpu_sample_forward(threads, repeats=1)
+        vals.append(v)
+        secs.append(t)
+    value = statistics.mean(vals)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000 * statistics.mean(secs), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "sage-mean-3layer-rmat-2450000n-62000000e",
+                   "sample": "1/64 of the workload", "threads": threads},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": ("the reference is TypeScript and no JS runtime exists on this image; the "
+                 "reference arm times the C restatement of its CPU path (oracle/)"),
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-spmm", action="store_true")
+    args = ap.parse_args()
+    rank = env_int("RANK", 0)
+    world = env_int("WORLD_SIZE", 1)
+    local = env_int("LOCAL_RANK", 0)
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import browsergnn_b200 as bg
+    from browsergnn_b200 import synth
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device(f"cuda:{local}"))
+    bg.init_browsergnn({"device": local})
+    ctx = bg.get_context(local)
+    hbm_peak, peak_kind = peaks()
+
+    n, e, scale = synth.SAGE_N, synth.SAGE_E, synth.SAGE_SCALE
+    seed = synth.seed_for(4)
+    ei = synth.rmat_edges_gpu(scale, n, e, seed, device=local)
+    gen = torch.Generator("cuda").manual_seed(seed)
+    x_full = torch.randn((n, WIDTHS[0]), device="cuda", generator=gen)
+    weights = make_weights(seed)
+    layers = build_layers(weights, local)
+
+    t0 = time.perf_counter()
+    if world > 1:
+        part = Partition(ei, n, e, rank, world, local)
+        dg = part.graph
+        x = x_full[part.lo:part.hi].contiguous()
+        exchange = part.exchange_fn(ctx)
+    else:
+        from browsergnn_b200.graph import DeviceGraph
+
+        dg = DeviceGraph(ei, e, n, n, device=local)
+        x = x_full
+        exchange = None
+        part = None
+    torch.cuda.synchronize()
+    build_s = time.perf_counter() - t0
+    del x_full
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        sage_forward(layers, dg, x, exchange)
+    barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    timers = []
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    l0 = ctx.launches
+    barrier()
+    start.record()
+    for _ in range(args.steps):
+        sage_forward(layers, dg, x, exchange, timers)
+    stop.record()
+    barrier()
+    clocks = sampler.stop()
+    launches = (ctx.launches - l0)
+    ms_total = start.elapsed_time(stop)
+    if world > 1:
+        t = torch.tensor([ms_total], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total = float(t.item())
+    ms_step = ms_total / args.steps
+    value = 3 * e / (ms_step * 1e-3)  # whole-job: all ranks' edges / max time
+
+    # roofline of the dominant kernel: the F=256 aggregation (layers 2 and 3)
+    agg_ms = {}
+    for li, fin, a, b in timers:
+        agg_ms.setdefault((li, fin), []).append(a.elapsed_time(b))
+    n_dst = dg.num_dst
+    e_loc = dg.num_edges
+    f = 256
+    bytes_alg = 4 * (n_dst + 1) + 4 * e_loc + 4 * f * e_loc + 4 * f * n_dst
+    t256 = [m for (li, fin), v in agg_ms.items() if fin == 256 for m in v]
+    agg_avg_ms = statistics.mean(t256)
+    achieved = bytes_alg / (agg_avg_ms * 1e-3) / 1e9
+    traffic = profile_traffic("aggregate_mean_f256_sage_rmat") if world == 1 else None
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak,
+                "unit": "GB/s", "frac": round(achieved / hbm_peak, 3), "traffic": traffic,
+                "kernel": "aggregate mean F=256 (light+heavy rows, one launch pair)",
+                "bytes_model": "gather model: 4(N+1) + 4E + 4FE + 4FN",
+                "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
+                "launch_ms": round(agg_avg_ms, 3),
+                "per_layer_aggregate_ms": {f"L{li + 1}_F{fin}": round(statistics.mean(v), 3)
+                                           for (li, fin), v in sorted(agg_ms.items())}}
+
+    # e2e through the public API: host features + host edge index each step
+    e2e = None
+    if not args.no_e2e and world == 1:
+        ei_host = ei.cpu().pin_memory()
+        x_host = x.cpu().pin_memory()
+        e2e_times = []
+        out_bytes = 0
+        for i in range(args.warmup + args.steps):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            g = bg.GraphData(x=x_host.to("cuda", non_blocking=True), numNodes=n,
+                             numFeatures=WIDTHS[0], edgeIndex=ei_host.numpy().view(np.uint32),
+                             numEdges=e)
+            out = g
+            for li, lay in enumerate(layers):
+                out = lay.forward(out, _act="relu" if li < 2 else None)
+            res = out.x.cpu()
+            t1 = time.perf_counter()
+            out_bytes = res.numel() * 4
+            out.device_graph().close()
+            if i >= args.warmup:
+                e2e_times.append(t1 - t0)
+        e2e_s = statistics.mean(e2e_times)
+        e2e = {"value": 3 * e / e2e_s, "unit": UNIT,
+               "h2d_bytes_per_step": int(x_host.numel() * 4 + ei_host.numel() * 4),
+               "d2h_bytes_per_step": int(out_bytes), "ms_per_step": round(1000 * e2e_s, 3),
+               "includes": "H2D of features and edge index, device CSR build, 3 layers, D2H"}
+
+    cpu = None
+    if not args.no_cpu and rank == 0 and world == 1:
+        threads = os.cpu_count() or 1
+        v, desc, _, _ = cpu_sample_forward(threads)
+        cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": desc}
+
+    spmm = None
+    if not args.no_spmm and world == 1:
+        del dg
+        torch.cuda.empty_cache()
+        spmm = spmm_sweep(max(3, args.steps // 2), 3, hbm_peak)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "sage-mean-3layer-rmat-2450000n-62000000e",
+                       "widths": WIDTHS, "edges_per_layer": e, "layers": 3,
+                       "parallelism": f"row-partition x{world}" if world > 1 else "single",
+                       "l2": "inputs larger than L2 (no flush)", "math": "fast (f32 fma)",
+                       "graph_build_s": round(build_s, 3)},
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "clocks": clocks, "gpu_launches": launches,
+        }
+        if part is not None:
+            line["config"]["halo_rows_rank0"] = part.n_halo
+        if spmm is not None:
+            line["spmm_sweep"] = spmm
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -136,13 +136,17 @@ class GraphData:
                 # device-side validation (graph.ts:88-92) happens in the CSR build
                 self._dgraph = DeviceGraph(self.edgeIndex, e, n, n, device=ei.device.index)
         else:
-            arr = np.ascontiguousarray(np.asarray(ei, dtype=np.int64)).reshape(-1)
+            arr = np.asarray(ei)
+            if arr.dtype.kind not in "ui":
+                arr = arr.astype(np.int64)
+            arr = arr.reshape(-1)
             if arr.size != 2 * e:
                 raise ValueError(f"Edge index length {arr.size} doesn't match numEdges({e}) * 2")
-            bad = np.flatnonzero((arr >= n) | (arr < 0))
-            if bad.size:
+            # graph.ts:88-92: the first out-of-range entry in flat order
+            if arr.size and (int(arr.max()) >= n or int(arr.min()) < 0):
+                bad = np.flatnonzero((arr >= n) | (arr < 0))
                 raise ValueError(f"Edge index {arr[bad[0]]} out of bounds for {n} nodes")
-            self.edgeIndex = arr.astype(np.uint32)
+            self.edgeIndex = np.ascontiguousarray(arr, dtype=np.uint32)
             self.numEdges = e
             self._dgraph = cfg.get("_dgraph")
         self.batch = None if cfg.get("batch") is None else np.asarray(cfg["batch"], np.uint32)
