@@ -84,6 +84,7 @@ SIGNATURES = {
     "bgnn_aggregate": [_P, _P, _I, _P, _U32, _P],
     "bgnn_gcn_propagate": [_P, _P, _P, _U32, _I, _I, _P, _I, _D, _P],
     "bgnn_gat": [_P, _P, _P, _U32, _U32, _P, _P, _D, _I, _I, _P, _I, _D, _P],
+    "bgnn_gat_noalloc": [_P, _P, _P, _U32, _U32, _P, _P, _D, _I, _I, _P, _I, _D, _P],
     "bgnn_gin_aggregate": [_P, _P, _P, _U32, _F, _P],
     "bgnn_graph_spmm": [_P, _P, _P, _P, _U32, _P],
     "bgnn_linear": [_P, _P, _P, _U32, _U32, _U32, _P, _I, _D, _P],

@@ -18,6 +18,8 @@
 // Dropout is a training-time op (Math.random) and is not offered here.
 // The softmax keeps the reference's constant shift of 10 rather than a max
 // shift, so exp overflows exactly where the reference's does.
+#include <mutex>
+
 #include "bgnn_internal.cuh"
 
 namespace {
@@ -195,6 +197,106 @@ int bgnn_run_gat(bgnn_ctx* ctx, const bgnn_graph* g, const float* h, uint32_t he
   while (lpe < (int)heads) lpe <<= 1;
   a.lpe = lpe;
   a.slope = slope;
+  a.concat = concat;
+  a.tail = tail;
+  a.act = act;
+  a.act_param = act_param;
+  const int ko = (int)((od + 31) / 32);
+  if (ko <= 1) return launch_gat<1>(ctx, a);
+  if (ko <= 2) return launch_gat<2>(ctx, a);
+  if (ko <= 4) return launch_gat<4>(ctx, a);
+  return launch_gat<8>(ctx, a);
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free GAT: the same kernel, with its per-edge attention scratch
+// in a fixed device array instead of a stream-ordered allocation.
+//
+// For callers that must not allocate device memory once they are running:
+// an inference server that reserves its whole memory budget at start-up and
+// forbids allocation afterwards, or a host application (a Node-API addon
+// embedded in a JavaScript runtime, for instance) whose device memory is
+// owned by someone else.  The caller still provides every input and output.
+//
+// The array holds BGNN_GAT_NOALLOC_MAX_FLOATS floats (16 MiB); every GPU that
+// loads this library keeps it until the process exits.  A call needs
+// (edges + appended self-loops) * heads floats.  All calls share the one
+// array, so calls whose kernels overlap on the GPU race on it; the kernel
+// writes each slot before reading it, so nothing needs clearing between calls.
+// ---------------------------------------------------------------------------
+#define BGNN_GAT_NOALLOC_MAX_FLOATS (4u << 20)
+
+static __device__ __align__(256) float g_gat_noalloc_scratch[BGNN_GAT_NOALLOC_MAX_FLOATS];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[kMaxDevices] = {};
+
+// The array's name in host code is only a host-side stand-in; the device
+// address comes from cudaGetSymbolAddress, looked up once per device with
+// that device current (on the first call on the device).
+int noalloc_scratch(bgnn_ctx* ctx, float** out) {
+  if (ctx->device < 0 || ctx->device >= kMaxDevices)
+    return bgnn_set_error(ctx, BGNN_ERR_UNSUPPORTED, "device ordinal %d out of range", ctx->device);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[ctx->device]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_gat_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return bgnn_set_error(ctx, BGNN_ERR_CUDA, "cudaGetSymbolAddress(scratch) failed: %s",
+                            cudaGetErrorString(e));
+    g_noalloc_ptr[ctx->device] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[ctx->device];
+  return BGNN_OK;
+}
+}  // namespace
+
+extern "C" int bgnn_gat_noalloc(bgnn_ctx* ctx, const bgnn_graph* g, const float* h,
+                                uint32_t heads, uint32_t c, const float* att_src,
+                                const float* att_dst, double negative_slope, int concat,
+                                int add_self_loops, const float* bias, int act,
+                                double act_param, float* out) {
+  if (!ctx) return BGNN_ERR_INVALID_ARG;
+  BGNN_CUDA(ctx, cudaSetDevice(ctx->device));
+  BGNN_REQUIRE(ctx, g != nullptr, "NULL graph");
+  BGNN_REQUIRE(ctx, h && att_src && att_dst && out, "NULL argument");
+  BGNN_REQUIRE(ctx, act >= BGNN_ACT_NONE && act <= BGNN_ACT_LEAKY_RELU, "unknown activation %d", act);
+  BGNN_REQUIRE(ctx, heads > 0 && c > 0, "heads and channels must be positive");
+  if (heads > 32)
+    return bgnn_set_error(ctx, BGNN_ERR_UNSUPPORTED, "GAT supports up to 32 heads (got %u)", heads);
+  const uint32_t od = concat ? heads * c : c;
+  if (od > 256)
+    return bgnn_set_error(ctx, BGNN_ERR_UNSUPPORTED, "GAT output width %u exceeds 256", od);
+  BGNN_REQUIRE(ctx, g->n_src == g->n_dst, "GAT needs a square graph");
+  const int tail = (add_self_loops && !g->has_self_loops) ? 1 : 0;  // gat.ts:116-118
+  const uint64_t need = (g->num_edges + (tail ? g->n_dst : 0)) * (uint64_t)heads;
+  if (need > BGNN_GAT_NOALLOC_MAX_FLOATS)
+    return bgnn_set_error(ctx, BGNN_ERR_INVALID_ARG,
+                          "allocation-free GAT needs %llu scratch floats; the limit is %u "
+                          "((edges + self-loops) * heads)",
+                          (unsigned long long)need, BGNN_GAT_NOALLOC_MAX_FLOATS);
+  if (g->n_dst == 0) return BGNN_OK;
+  float* scratch = nullptr;
+  BGNN_TRY(noalloc_scratch(ctx, &scratch));
+  GatArgs a;
+  a.row_ptr = g->row_ptr;
+  a.src_of = g->src_of;
+  a.h = h;
+  a.att_src = att_src;
+  a.att_dst = att_dst;
+  a.bias = bias;
+  a.out = out;
+  a.scratch = scratch;
+  a.num_edges = g->num_edges;
+  a.n_rows = g->n_dst;
+  a.heads = (int)heads;
+  a.c = (int)c;
+  int lpe = 1;
+  while (lpe < (int)heads) lpe <<= 1;
+  a.lpe = lpe;
+  a.slope = negative_slope;
   a.concat = concat;
   a.tail = tail;
   a.act = act;

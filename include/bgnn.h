@@ -202,6 +202,21 @@ BGNN_API int bgnn_gcn_propagate(bgnn_ctx* ctx, const bgnn_graph* g, const float*
 BGNN_API int bgnn_gat(bgnn_ctx* ctx, const bgnn_graph* g, const float* h, uint32_t heads, uint32_t c,
              const float* att_src, const float* att_dst, double negative_slope, int concat,
              int add_self_loops, const float* bias, int act, double act_param, float* out);
+/* bgnn_gat without any device allocation (no counterpart in the reference).
+ * For callers that must not allocate once running -- an inference server
+ * that reserves its memory budget at start-up, or a host application (such as
+ * a Node-API addon inside a JavaScript runtime) whose device memory belongs to
+ * someone else.  Same arguments and results as bgnn_gat; its per-edge
+ * attention scratch lives in a fixed 16 MiB device array that every GPU
+ * loading this library keeps until exit, so (edges + appended self-loops) *
+ * heads must not exceed 4,194,304 (larger graphs get BGNN_ERR_INVALID_ARG).
+ * The first call on a device looks up the array's device address; make that
+ * first call before any stream capture begins.  All calls share the array:
+ * calls that overlap on the GPU race on it. */
+BGNN_API int bgnn_gat_noalloc(bgnn_ctx* ctx, const bgnn_graph* g, const float* h, uint32_t heads,
+                              uint32_t c, const float* att_src, const float* att_dst,
+                              double negative_slope, int concat, int add_self_loops,
+                              const float* bias, int act, double act_param, float* out);
 /* GINConv step 1-3 (gin.ts:131-157): out = f32((1+eps)*x + sum_j x_j). */
 BGNN_API int bgnn_gin_aggregate(bgnn_ctx* ctx, const bgnn_graph* g, const float* x,
                        uint32_t num_features, float eps, float* out);
