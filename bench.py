@@ -186,80 +186,6 @@ def sage_forward(layers, dg, x, exchange=None, timers=None):
 
 
 # ---------------------------------------------------------------------------
-# partitioning (N > 1)
-# ---------------------------------------------------------------------------
-class Partition:
-    """Destination-row partition of the graph with a halo plan (built once)."""
-
-    def __init__(self, ei, n, e, rank, world, device):
-        import torch
-        import torch.distributed as dist
-
-        from browsergnn_b200.graph import DeviceGraph
-
-        src = ei[:e].long()
-        dst = ei[e:].long()
-        src[src < 0] += 1 << 32
-        dst[dst < 0] += 1 << 32
-        indeg = torch.bincount(dst, minlength=n)
-        cum = torch.cumsum(indeg, 0)
-        # contiguous row ranges with ~E/world edges each
-        targets = torch.arange(1, world, device=cum.device) * (e / world)
-        cuts = torch.searchsorted(cum.double(), targets.double()).tolist()
-        bounds = [0] + [int(c) + 1 for c in cuts] + [n]
-        for i in range(1, len(bounds)):
-            bounds[i] = max(bounds[i], bounds[i - 1])
-        self.bounds = bounds
-        lo, hi = bounds[rank], bounds[rank + 1]
-        self.lo, self.hi, self.n_own = lo, hi, hi - lo
-        keep = (dst >= lo) & (dst < hi)  # COO order preserved: stable per row
-        ls, ld = src[keep], dst[keep] - lo
-        own = (ls >= lo) & (ls < hi)
-        halo = torch.unique(ls[~own])  # sorted global ids
-        self.n_halo = int(halo.numel())
-        col = torch.empty_like(ls)
-        col[own] = ls[own] - lo
-        col[~own] = self.n_own + torch.searchsorted(halo, ls[~own])
-        self.e_local = int(ls.numel())
-        local_ei = torch.cat([col, ld]).to(torch.int64)
-        local_ei = torch.where(local_ei >= (1 << 31), local_ei - (1 << 32), local_ei).to(torch.int32)
-        self.graph = DeviceGraph(local_ei, self.e_local, self.n_own + self.n_halo, self.n_own,
-                                 device=device)
-        # requests: halo ids grouped by owner (ranges are increasing, halo sorted)
-        owner = torch.searchsorted(torch.tensor(bounds[1:], device=halo.device), halo, right=True)
-        send_req = torch.bincount(owner, minlength=world).to(torch.int64)
-        recv_req = torch.empty_like(send_req)
-        dist.all_to_all_single(recv_req, send_req)
-        self.recv_splits = send_req.tolist()   # rows I receive from each rank
-        self.send_splits = recv_req.tolist()   # rows I send to each rank
-        req_ids = torch.empty(sum(self.send_splits), dtype=torch.int64, device=halo.device)
-        dist.all_to_all_single(req_ids, halo.to(torch.int64), self.send_splits, self.recv_splits)
-        self.send_rows = (req_ids - lo).to(torch.int32).contiguous()
-        self.n_send = int(self.send_rows.numel())
-        self.x_local = None
-
-    def exchange_fn(self, ctx):
-        import torch
-        import torch.distributed as dist
-
-        from browsergnn_b200.backend import ptr
-
-        def exchange(h):
-            f = h.shape[1]
-            ext = torch.empty((self.n_own + self.n_halo, f), dtype=torch.float32, device=h.device)
-            ext[: self.n_own].copy_(h)
-            send = torch.empty((self.n_send, f), dtype=torch.float32, device=h.device)
-            if self.n_send:
-                ctx.call("bgnn_pack_rows", ptr(h), self.n_own, ptr(self.send_rows), self.n_send, f,
-                         ptr(send))
-            recv = ext[self.n_own:]
-            dist.all_to_all_single(recv, send, self.recv_splits, self.send_splits)
-            return ext
-
-        return exchange
-
-
-# ---------------------------------------------------------------------------
 # SpMM sweep (standalone CSR SpMM, scale-24 R-MAT, 2^28 edges)
 # ---------------------------------------------------------------------------
 def spmm_sweep(steps, warmup, hbm_peak):
@@ -428,10 +354,13 @@ def main():
 
     t0 = time.perf_counter()
     if world > 1:
-        part = Partition(ei, n, e, rank, world, local)
-        dg = part.graph
+        from browsergnn_b200.partition import HaloPlan, cuda_pack
+
+        part = HaloPlan(ei[:e], ei[e:], n, rank, world)
+        dg = part.device_graph(local)
         x = x_full[part.lo:part.hi].contiguous()
-        exchange = part.exchange_fn(ctx)
+        pack = cuda_pack(ctx)
+        exchange = lambda h: part.exchange(h, pack)  # noqa: E731
     else:
         from browsergnn_b200.graph import DeviceGraph
 

@@ -261,6 +261,237 @@ __global__ void __launch_bounds__(HV_THREADS) k_agg_heavy(const AggArgs a, int v
 }
 
 // ---------------------------------------------------------------------------
+// streaming schedule: a persistent kernel over the graph's work items.
+//
+// A "pipe" is a group of threads that streams one item (a heavy row, or a run
+// of consecutive light rows) through a 3-stage cp.async ring in shared
+// memory: every thread of the pipe copies the source-row slices of its edge,
+// and thread f (f < slice width) accumulates feature f over the item's edges
+// in CSR order, writing a row out when the edge stream crosses the row's end.
+// Phase 1 runs the heavy items (largest first) with the whole CTA as one pipe;
+// phase 2 splits the CTA into P pipes (P = 256 / padded width) that pull light
+// items from a queue.  Items are fetched with one atomic per item.
+// ---------------------------------------------------------------------------
+constexpr int ST_THREADS = 256;
+constexpr int ST_S = 3;       // ring stages
+constexpr int ST_EPS = 32;    // edges per stage per light pipe
+constexpr int ST_RMAX = 256;  // rows per light item (the graph's schedule builder cuts at this)
+constexpr int ST_SW = 256;    // features per slice
+
+__device__ __forceinline__ void pipe_bar(int id, int count) {
+  if (id == 0)
+    __syncthreads();
+  else
+    asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
+}
+
+template <int OP>
+__device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint32_t re, int f0,
+                                             int fw, int vec4, int swp, int tp, int ptid, int eps,
+                                             float* buf, float* wbuf, uint32_t* sidx, uint32_t* rps,
+                                             float* rdv,
+                                             int bar_id) {
+  const uint32_t e0 = a.row_ptr[rb];
+  const uint32_t ne = a.row_ptr[re] - e0;
+  const uint32_t nrows = re - rb;
+  for (uint32_t i = ptid; i <= nrows; i += tp) rps[i] = a.row_ptr[rb + i] - e0;
+  if (OP == OP_GCN)
+    for (uint32_t i = ptid; i < nrows; i += tp) rdv[i] = a.dinv[rb + i];
+  pipe_bar(bar_id, tp);
+
+  const int cpe = vec4 ? (fw >> 2) : fw;  // 16- or 4-byte copies per edge
+  const int copies = eps * cpe;
+  const uint32_t nst = (ne + eps - 1) / eps;
+  constexpr uint32_t NONE = 0xffffffffu;
+  // source ids of stage k live in sidx[k % (S+1)], loaded two iterations
+  // before the stage is issued so no copy waits on an index load
+  auto src_for = [&](uint32_t k) -> uint32_t {
+    const uint32_t e = k * (uint32_t)eps + (uint32_t)ptid;
+    return (ptid < eps && k < nst && e < ne) ? a.src_of[e0 + e] : NONE;
+  };
+  auto issue = [&](uint32_t k) {
+    if (k < nst) {
+      const int slot = (int)(k % ST_S);
+      const uint32_t* sid = sidx + (k % (ST_S + 1)) * eps;
+      float* sb = buf + (size_t)slot * eps * swp;
+      // consecutive threads copy consecutive chunks of the same source row
+      for (int c = ptid; c < copies; c += tp) {
+        const int j = c / cpe;
+        const int q = c - j * cpe;
+        const uint32_t s = sid[j];
+        if (s == NONE) break;  // edges past the end: later c only go further
+        if (vec4)
+          cp_async16(sb + (size_t)j * swp + 4 * q, a.x + (int64_t)s * a.ld_x + f0 + 4 * q);
+        else
+          cp_async4(sb + (size_t)j * swp + q, a.x + (int64_t)s * a.ld_x + f0 + q);
+      }
+      if (ptid < eps) {
+        const uint32_t s = sid[ptid];
+        if (s != NONE) {
+          float* w = wbuf + slot * eps + ptid;
+          if (OP == OP_GCN) cp_async4(w, a.dinv + s);
+          if (OP == OP_SPMM || OP == OP_SPMM_X) cp_async4(w, a.val + e0 + k * (uint32_t)eps + ptid);
+        }
+      }
+    }
+    cp_async_commit();
+  };
+
+  if (ptid < eps) {
+#pragma unroll
+    for (int k = 0; k <= ST_S; k++) sidx[k * eps + ptid] = src_for((uint32_t)k);
+  }
+  pipe_bar(bar_id, tp);
+#pragma unroll
+  for (int k = 0; k < ST_S - 1; k++) issue((uint32_t)k);
+  const bool consumer = ptid < fw;
+  float acc = init_acc<OP>();
+  uint32_t r = 0;
+  uint32_t nxt = rps[1];
+  float dinv_r = (OP == OP_GCN && nrows) ? rdv[0] : 0.0f;
+  auto finalize = [&]() {
+    const uint32_t row = rb + r;
+    const int f = f0 + ptid;
+    a.out[(int64_t)row * a.ld_out + f] = epilogue(acc, a, row, f, rps[r + 1] - rps[r]);
+    acc = init_acc<OP>();
+    r++;
+    if (r < nrows) {
+      nxt = rps[r + 1];
+      if (OP == OP_GCN) dinv_r = rdv[r];
+    }
+  };
+  for (uint32_t k = 0; k < nst; k++) {
+    cp_async_wait<ST_S - 2>();
+    pipe_bar(bar_id, tp);
+    issue(k + ST_S - 1);
+    const uint32_t s_ahead = src_for(k + ST_S + 1);
+    if (consumer) {
+      const int slot = (int)(k % ST_S);
+      const float* b = buf + (size_t)slot * eps * swp + ptid;
+      const float* wb = wbuf + slot * eps;
+      const uint32_t base = k * (uint32_t)eps;
+      const uint32_t cnt = min((uint32_t)eps, ne - base);
+      constexpr int UB = 8;
+      uint32_t j = 0;
+      for (; j + UB <= cnt; j += UB) {
+        // issue the block's shared-memory reads first, then reduce in order
+        float v[UB], wr[UB];
+#pragma unroll
+        for (int u = 0; u < UB; u++) {
+          v[u] = b[(size_t)(j + u) * swp];
+          wr[u] = (OP == OP_GCN || OP == OP_SPMM || OP == OP_SPMM_X) ? wb[j + u] : 0.0f;
+        }
+        if (nxt >= base + j + UB) {  // no row ends inside this block
+#pragma unroll
+          for (int u = 0; u < UB; u++) {
+            const float w = (OP == OP_GCN) ? __fmul_rn(wr[u], dinv_r) : wr[u];
+            acc = step<OP>(acc, v[u], w);
+          }
+        } else {
+#pragma unroll
+          for (int u = 0; u < UB; u++) {
+            while (base + j + u == nxt) finalize();
+            const float w = (OP == OP_GCN) ? __fmul_rn(wr[u], dinv_r) : wr[u];
+            acc = step<OP>(acc, v[u], w);
+          }
+        }
+      }
+      for (; j < cnt; j++) {
+        while (base + j == nxt) finalize();
+        float w = 0.0f;
+        if (OP == OP_GCN) w = __fmul_rn(wb[j], dinv_r);
+        if (OP == OP_SPMM || OP == OP_SPMM_X) w = wb[j];
+        acc = step<OP>(acc, b[(size_t)j * swp], w);
+      }
+    }
+    // stage k+S+1's ids go to the slot stage k+S+1 - (S+1) = k used; stage k
+    // was issued two iterations ago and nobody reads that slot again
+    if (ptid < eps) sidx[((k + ST_S + 1) % (ST_S + 1)) * eps + ptid] = s_ahead;
+  }
+  cp_async_wait<0>();
+  if (consumer)
+    while (r < nrows) finalize();
+  pipe_bar(bar_id, tp);  // the ring and row buffer are reused by the next item
+}
+
+template <int OP>
+__global__ void __launch_bounds__(ST_THREADS, 2)
+    k_agg_stream(const AggArgs a, int P, int swp, int n_slices, int vec4, uint32_t* queue) {
+  extern __shared__ float4 st_smem4[];
+  float* data = reinterpret_cast<float*>(st_smem4);
+  const size_t data_f = (size_t)P * ST_S * ST_EPS * swp;
+  float* wb = data + data_f;
+  uint32_t* sidx = reinterpret_cast<uint32_t*>(wb + P * ST_S * ST_EPS);
+  uint32_t* rps = sidx + P * (ST_S + 1) * ST_EPS;
+  uint32_t* slots = rps + P * (ST_RMAX + 1);
+  float* rdv = reinterpret_cast<float*>(slots + 16);  // present for OP_GCN only
+  const int F = a.num_features;
+  const uint32_t heavy_work = a.n_heavy_items * (uint32_t)n_slices;
+  const uint32_t light_work = (a.n_items - a.n_heavy_items) * (uint32_t)n_slices;
+
+  // phase 1: heavy rows, the whole CTA as one pipe
+  for (;;) {
+    if (threadIdx.x == 0) slots[P] = atomicAdd(&queue[0], 1u);
+    __syncthreads();
+    const uint32_t w = slots[P];
+    if (w >= heavy_work) break;
+    const uint2 item = a.items[w / (uint32_t)n_slices];
+    const int f0 = (int)(w % (uint32_t)n_slices) * ST_SW;
+    stream_range<OP>(a, item.x, item.y, f0, min(ST_SW, F - f0), vec4, swp, ST_THREADS,
+                     threadIdx.x, ST_EPS * P, data, wb, sidx, rps, rdv, 0);
+  }
+  // phase 2: light items, P independent pipes
+  const int tp = ST_THREADS / P;
+  const int pipe = threadIdx.x / tp, ptid = threadIdx.x % tp;
+  const int bar_id = P == 1 ? 0 : pipe + 1;
+  float* pdata = data + (size_t)pipe * ST_S * ST_EPS * swp;
+  float* pwb = wb + pipe * ST_S * ST_EPS;
+  uint32_t* psidx = sidx + pipe * (ST_S + 1) * ST_EPS;
+  uint32_t* prps = rps + pipe * (ST_RMAX + 1);
+  float* prdv = rdv + pipe * ST_RMAX;
+  for (;;) {
+    if (ptid == 0) slots[pipe] = atomicAdd(&queue[1], 1u);
+    pipe_bar(bar_id, tp);
+    const uint32_t w = slots[pipe];
+    if (w >= light_work) break;
+    const uint2 item = a.items[a.n_heavy_items + w / (uint32_t)n_slices];
+    const int f0 = (int)(w % (uint32_t)n_slices) * ST_SW;
+    stream_range<OP>(a, item.x, item.y, f0, min(ST_SW, F - f0), vec4, swp, tp, ptid, ST_EPS,
+                     pdata, pwb, psidx, prps, prdv, bar_id);
+  }
+}
+
+template <int OP>
+int launch_stream(bgnn_ctx* ctx, const AggArgs& a) {
+  const int F = a.num_features;
+  const int fs = F < ST_SW ? F : ST_SW;
+  const int swp = (fs + 3) & ~3;
+  int pw = 32;
+  while (pw < swp) pw <<= 1;
+  const int P = ST_THREADS / pw;  // 1, 2, 4 or 8
+  const int n_slices = (F + ST_SW - 1) / ST_SW;
+  const bool vec4 = (F % 4 == 0) && ((uintptr_t)a.x % 16 == 0) && (a.ld_x % 4 == 0);
+  size_t smem = ((size_t)P * ST_S * ST_EPS * swp + (size_t)P * ST_S * ST_EPS) * 4 +
+                (size_t)(P * (ST_S + 1) * ST_EPS + P * (ST_RMAX + 1) + 16) * 4;
+  if (OP == OP_GCN) smem += (size_t)P * ST_RMAX * 4;
+  BGNN_CUDA(ctx, cudaFuncSetAttribute(k_agg_stream<OP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)smem));
+  int per_sm = 0;
+  BGNN_CUDA(ctx, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_agg_stream<OP>,
+                                                               ST_THREADS, smem));
+  if (per_sm < 1) per_sm = 1;
+  const uint64_t work = (uint64_t)a.n_items * n_slices;
+  uint64_t grid = (uint64_t)ctx->num_sms * per_sm;
+  if (grid > work) grid = work ? work : 1;
+  uint32_t* queue = ctx->d_small;
+  BGNN_CUDA(ctx, cudaMemsetAsync(queue, 0, 2 * sizeof(uint32_t), ctx->stream));
+  k_agg_stream<OP><<<(unsigned)grid, ST_THREADS, smem, ctx->stream>>>(a, P, swp, n_slices,
+                                                                      vec4 ? 1 : 0, queue);
+  BGNN_LAUNCHED(ctx);
+  return BGNN_OK;
+}
+
+// ---------------------------------------------------------------------------
 // host dispatch
 // ---------------------------------------------------------------------------
 template <int OP, int V, int CH>
@@ -297,6 +528,9 @@ template <int OP>
 int run_op(bgnn_ctx* ctx, const AggArgs& a0) {
   AggArgs a = a0;
   const int F = a.num_features;
+  // the streaming schedule covers every case except the appended self-loop
+  // edge (GCN/GAT loop insertion), which the light/heavy pair handles
+  if (!a.tail && a.items != nullptr && a.n_items > 0) return launch_stream<OP>(ctx, a);
   const bool al_x = ((uintptr_t)a.x % 16 == 0) && (a.ld_x % 4 == 0);
   const bool al_o = ((uintptr_t)a.out % 16 == 0) && (a.ld_out % 4 == 0);
   const int V = (F % 4 == 0 && al_x && al_o) ? 4 : 1;

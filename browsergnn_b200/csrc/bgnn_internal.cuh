@@ -36,9 +36,14 @@ struct bgnn_graph {
   uint32_t* src_of = nullptr;      // [E] source node of each CSR slot
   uint32_t* eid = nullptr;         // [E] COO edge id of each CSR slot
   uint32_t* out_deg = nullptr;     // [n_src]
-  uint32_t* heavy_rows = nullptr;  // rows handled CTA-per-row
+  uint32_t* heavy_rows = nullptr;  // rows handled CTA-per-row, largest first
   uint32_t n_heavy = 0;
   uint32_t heavy_threshold = 0;
+  // streaming schedule: work items [row_begin, row_end): first every heavy
+  // row on its own (largest first), then runs of consecutive light rows
+  uint2* items = nullptr;
+  uint32_t n_items = 0;
+  uint32_t n_heavy_items = 0;
   int has_self_loops = 0;
   bool csr_only = false;           // built from an existing CSR (no eid/out_deg)
   float* dinv[2] = {nullptr, nullptr};  // GCN D^-1/2 without / with loop tail
@@ -156,6 +161,9 @@ struct AggArgs {
   const uint32_t* heavy_rows;
   uint32_t n_heavy;
   uint32_t heavy_threshold;
+  const uint2* items;     // streaming schedule (NULL: use the light/heavy pair)
+  uint32_t n_items;
+  uint32_t n_heavy_items;
   int tail;               // virtual self-loop edge after each row's edges
   int mean;               // sum * (1/count)
   int max_fix;            // -inf -> 0

@@ -44,6 +44,9 @@ AggArgs graph_args(const bgnn_graph* g, const float* x, uint32_t f, float* out) 
   a.heavy_rows = g->heavy_rows;
   a.n_heavy = g->n_heavy;
   a.heavy_threshold = g->heavy_threshold;
+  a.items = g->items;
+  a.n_items = g->n_items;
+  a.n_heavy_items = g->n_heavy_items;
   a.gin_ope = 1.0;
   a.act = BGNN_ACT_NONE;
   return a;

@@ -60,18 +60,6 @@ __global__ void k_count_validate(const uint32_t* __restrict__ src, const uint32_
   }
 }
 
-__global__ void k_count_heavy(const uint32_t* __restrict__ row_ptr, uint32_t n_rows,
-                              uint32_t threshold, uint32_t* __restrict__ list, uint32_t cap,
-                              uint32_t* __restrict__ counter) {
-  for (uint32_t r = blockIdx.x * blockDim.x + threadIdx.x; r < n_rows;
-       r += gridDim.x * blockDim.x) {
-    if (row_ptr[r + 1] - row_ptr[r] >= threshold) {
-      const uint32_t p = atomicAdd(counter, 1u);
-      if (p < cap) list[p] = r;
-    }
-  }
-}
-
 // D^-1/2 from the CSR degree: the reference counts degrees in a Float32Array
 // (+1 per edge, saturating at 2^24) and stores f32(1/Math.sqrt(deg)).
 __global__ void k_dinv_from_rowptr(const uint32_t* __restrict__ row_ptr, uint32_t n, int tail,
@@ -126,36 +114,69 @@ int counts_to_rowptr(bgnn_ctx* ctx, uint32_t* counts_then_rowptr, uint32_t n_row
   return bgnn_exclusive_scan(ctx, counts_then_rowptr, counts_then_rowptr, (uint64_t)n_rows + 1);
 }
 
-int collect_heavy(bgnn_ctx* ctx, bgnn_graph* g) {
-  g->heavy_threshold = 256;
+// Row schedule, built once per graph on the host from a copy of row_ptr:
+//  * heavy rows (degree >= 256), largest first, for the CTA-per-row kernel;
+//  * streaming work items: every heavy row alone (largest first), then runs
+//    of consecutive light rows holding up to kItemEdges edges and
+//    kItemRows rows.  Items never split a row, so each row is still reduced
+//    by one pipe in edge order.
+constexpr uint32_t kHeavyThreshold = 256;
+constexpr uint32_t kItemEdges = 1024;
+constexpr uint32_t kItemRows = 256;  // must equal the streaming kernel's row buffer
+
+int build_schedule(bgnn_ctx* ctx, bgnn_graph* g) {
+  g->heavy_threshold = kHeavyThreshold;
   g->n_heavy = 0;
-  if (g->num_edges < g->heavy_threshold || g->n_dst == 0) return BGNN_OK;
-  const uint64_t cap64 = g->num_edges / g->heavy_threshold + 1;
-  const uint32_t cap = (uint32_t)std::min<uint64_t>(cap64, g->n_dst);
-  DevTmp list;
-  BGNN_TRY(bgnn_tmp_alloc(ctx, list, (uint64_t)cap * 4));
-  BGNN_CUDA(ctx, cudaMemsetAsync(ctx->d_small, 0, 4, ctx->stream));
-  k_count_heavy<<<grid_for(ctx, g->n_dst, 256), 256, 0, ctx->stream>>>(
-      g->row_ptr, g->n_dst, g->heavy_threshold, list.as<uint32_t>(), cap, ctx->d_small);
-  BGNN_LAUNCHED(ctx);
-  uint32_t count = 0;
-  BGNN_CUDA(ctx, cudaMemcpyAsync(&count, ctx->d_small, 4, cudaMemcpyDeviceToHost, ctx->stream));
+  g->n_items = 0;
+  g->n_heavy_items = 0;
+  const uint32_t n = g->n_dst;
+  if (n == 0) return BGNN_OK;
+  std::vector<uint32_t> rp((size_t)n + 1);
+  BGNN_CUDA(ctx, cudaMemcpyAsync(rp.data(), g->row_ptr, ((size_t)n + 1) * 4,
+                                 cudaMemcpyDeviceToHost, ctx->stream));
   BGNN_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
-  if (count == 0) return BGNN_OK;
-  count = std::min(count, cap);
-  // order heavy rows by degree, largest first, so the longest rows start first
-  std::vector<uint32_t> rows(count), rp_lo(count), rp_hi(count);
-  BGNN_CUDA(ctx, cudaMemcpy(rows.data(), list.p, count * 4, cudaMemcpyDeviceToHost));
-  std::vector<uint32_t> rp(g->n_dst + 1);
-  BGNN_CUDA(ctx, cudaMemcpy(rp.data(), g->row_ptr, ((size_t)g->n_dst + 1) * 4,
-                            cudaMemcpyDeviceToHost));
-  std::sort(rows.begin(), rows.end(), [&](uint32_t a, uint32_t b) {
+  std::vector<uint32_t> heavy;
+  for (uint32_t r = 0; r < n; r++)
+    if (rp[r + 1] - rp[r] >= kHeavyThreshold) heavy.push_back(r);
+  std::sort(heavy.begin(), heavy.end(), [&](uint32_t a, uint32_t b) {
     const uint32_t da = rp[a + 1] - rp[a], db = rp[b + 1] - rp[b];
     return da != db ? da > db : a < b;
   });
-  BGNN_CUDA(ctx, cudaMalloc(&g->heavy_rows, (size_t)count * 4));
-  BGNN_CUDA(ctx, cudaMemcpy(g->heavy_rows, rows.data(), (size_t)count * 4, cudaMemcpyHostToDevice));
-  g->n_heavy = count;
+  std::vector<uint2> items;
+  items.reserve(heavy.size() + n / 64 + 16);
+  for (uint32_t r : heavy) items.push_back(make_uint2(r, r + 1));
+  uint32_t begin = 0, edges = 0;
+  bool open = false;
+  for (uint32_t r = 0; r < n; r++) {
+    const uint32_t d = rp[r + 1] - rp[r];
+    if (d >= kHeavyThreshold) {
+      if (open) items.push_back(make_uint2(begin, r));
+      open = false;
+      continue;
+    }
+    if (!open) {
+      begin = r;
+      edges = 0;
+      open = true;
+    }
+    edges += d;
+    if (edges >= kItemEdges || r + 1 - begin >= kItemRows) {
+      items.push_back(make_uint2(begin, r + 1));
+      open = false;
+    }
+  }
+  if (open) items.push_back(make_uint2(begin, n));
+  if (!heavy.empty()) {
+    BGNN_CUDA(ctx, cudaMalloc(&g->heavy_rows, heavy.size() * 4));
+    BGNN_CUDA(ctx, cudaMemcpy(g->heavy_rows, heavy.data(), heavy.size() * 4,
+                              cudaMemcpyHostToDevice));
+    g->n_heavy = (uint32_t)heavy.size();
+  }
+  BGNN_CUDA(ctx, cudaMalloc(&g->items, items.size() * sizeof(uint2)));
+  BGNN_CUDA(ctx, cudaMemcpy(g->items, items.data(), items.size() * sizeof(uint2),
+                            cudaMemcpyHostToDevice));
+  g->n_items = (uint32_t)items.size();
+  g->n_heavy_items = (uint32_t)heavy.size();
   return BGNN_OK;
 }
 
@@ -168,6 +189,7 @@ void bgnn_graph_free(bgnn_graph* g) {
   cudaFree(g->eid);
   cudaFree(g->out_deg);
   cudaFree(g->heavy_rows);
+  cudaFree(g->items);
   cudaFree(g->dinv[0]);
   cudaFree(g->dinv[1]);
   *g = bgnn_graph();
@@ -217,7 +239,7 @@ int bgnn_graph_build(bgnn_ctx* ctx, const uint32_t* src, const uint32_t* dst, ui
   const int bits = n_dst > 1 ? bgnn_bits_for(n_dst - 1) : 0;
   BGNN_TRY(bgnn_radix_sort_pairs(ctx, dst, nullptr, E, bits, nullptr, g->eid));
   BGNN_TRY(bgnn_gather_u32(ctx, src, g->eid, E, g->src_of));
-  BGNN_TRY(collect_heavy(ctx, g));
+  BGNN_TRY(build_schedule(ctx, g));
   return BGNN_OK;
 }
 
@@ -262,7 +284,7 @@ int bgnn_graph_from_csr(bgnn_ctx* ctx, const uint32_t* row_ptr, const uint32_t* 
     return bgnn_set_error(ctx, BGNN_ERR_OUT_OF_RANGE,
                           "column index out of bounds for %u columns (position %llu)", num_cols,
                           hb[0]);
-  BGNN_TRY(collect_heavy(ctx, g));
+  BGNN_TRY(build_schedule(ctx, g));
   return BGNN_OK;
 }
 

@@ -152,6 +152,38 @@ def test_aggregate_bit_exact(bg, torch, aggr, f):
     assert_bits_equal(out.cpu().numpy(), want, f"{aggr} F={f}")
 
 
+@pytest.mark.parametrize("case", ["no_edges", "one_hub", "all_heavy", "long_empty_runs"])
+@pytest.mark.parametrize("f", [32, 100])
+def test_aggregate_schedule_edge_cases(bg, torch, case, f):
+    rng = np.random.default_rng(3)
+    if case == "no_edges":
+        n, src, dst = 700, np.zeros(0, np.int64), np.zeros(0, np.int64)
+    elif case == "one_hub":
+        n = 600
+        src = rng.integers(0, n, 20000)
+        dst = np.full(20000, 17)
+    elif case == "all_heavy":
+        n = 40
+        src = rng.integers(0, n, 40 * 300)
+        dst = np.repeat(np.arange(n), 300)[rng.permutation(40 * 300)]
+    else:
+        n = 5000  # a few edges, thousands of empty rows between them
+        src = rng.integers(0, n, 50)
+        dst = rng.integers(0, n, 50)
+    ei = np.concatenate([src, dst]).astype(np.uint32)
+    e = src.size
+    x = rng.standard_normal((n, f)).astype(np.float32)
+    g = bg.GraphData(x=x, numNodes=n, numFeatures=f, edgeIndex=ei, numEdges=e)
+    dg = g.device_graph()
+    for aggr, code in (("sum", 0), ("mean", 1), ("max", 2)):
+        out = torch.empty((n, f), dtype=torch.float32, device="cuda")
+        dg.ctx.call("bgnn_aggregate", dg.h, code, g.x_device().data_ptr(), f, out.data_ptr())
+        gathered = orc.gather(x, ei[:e], f)
+        want = {"sum": orc.scatter_add, "mean": orc.scatter_mean,
+                "max": orc.scatter_max}[aggr](gathered, ei[e:], n, f)
+        assert_bits_equal(out.cpu().numpy(), want, f"{case} {aggr} F={f}")
+
+
 @pytest.mark.parametrize("aggr", ["sum", "mean", "max"])
 def test_scatter_facade_bit_exact(bg, torch, aggr):
     rng = np.random.default_rng(7)
