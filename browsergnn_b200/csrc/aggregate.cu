@@ -184,6 +184,52 @@ __device__ __forceinline__ void cp_async4(void* s, const void* g) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(sa), "l"(g) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+
+// ---- mbarrier + bulk copy (TMA engine, non-tensor form) ----------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, int count) {
+  const unsigned a = (unsigned)__cvta_generic_to_shared(bar);
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(a), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(unsigned bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+// global -> shared bulk copy completing `bytes` on the mbarrier (no multicast)
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, unsigned bar) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(d),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(unsigned bar, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Waits for the phase with the given parity to complete; gives up after about
+// 2^32 SM cycles (~2 s) so a lost copy can never hang the GPU.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
+  const unsigned a = (unsigned)__cvta_generic_to_shared(bar);
+  if (mbar_try_wait(a, parity)) return true;
+  const long long t0 = clock64();
+  for (;;) {
+    if (mbar_try_wait(a, parity)) return true;
+    if (clock64() - t0 > (1ll << 32)) return false;
+  }
+}
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
@@ -285,11 +331,27 @@ __device__ __forceinline__ void pipe_bar(int id, int count) {
     asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
 }
 
-template <int OP>
-__device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint32_t re, int f0,
-                                             int fw, int vec4, int swp, int tp, int ptid, int eps,
+// barrier that also returns the OR of `pred` over the pipe's threads, so every
+// thread takes the same decision
+__device__ __forceinline__ bool pipe_bar_or(int id, int count, bool pred) {
+  if (id == 0) return __syncthreads_or(pred ? 1 : 0) != 0;
+  unsigned r;
+  asm volatile(
+      "{\n\t.reg .pred q, p;\n\t"
+      "setp.ne.u32 q, %1, 0;\n\t"
+      "barrier.red.or.pred p, %2, %3, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(r)
+      : "r"(pred ? 1u : 0u), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
+}
+
+template <int OP, bool BULK>
+__device__ __forceinline__ bool stream_range(const AggArgs& a, uint32_t rb, uint32_t re, int f0,
+                                             int fw, int swp, int tp, int ptid, int eps,
                                              float* buf, float* wbuf, uint32_t* sidx, uint32_t* rps,
-                                             float* rdv,
+                                             float* rdv, uint64_t* mbar, uint32_t& kg,
                                              int bar_id) {
   const uint32_t e0 = a.row_ptr[rb];
   const uint32_t ne = a.row_ptr[re] - e0;
@@ -297,11 +359,9 @@ __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint
   for (uint32_t i = ptid; i <= nrows; i += tp) rps[i] = a.row_ptr[rb + i] - e0;
   if (OP == OP_GCN)
     for (uint32_t i = ptid; i < nrows; i += tp) rdv[i] = a.dinv[rb + i];
-  pipe_bar(bar_id, tp);
 
-  const int cpe = vec4 ? (fw >> 2) : fw;  // 16- or 4-byte copies per edge
-  const int copies = eps * cpe;
   const uint32_t nst = (ne + eps - 1) / eps;
+  const uint32_t row_bytes = (uint32_t)fw * 4u;
   constexpr uint32_t NONE = 0xffffffffu;
   // source ids of stage k live in sidx[k % (S+1)], loaded two iterations
   // before the stage is issued so no copy waits on an index load
@@ -309,21 +369,32 @@ __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint
     const uint32_t e = k * (uint32_t)eps + (uint32_t)ptid;
     return (ptid < eps && k < nst && e < ne) ? a.src_of[e0 + e] : NONE;
   };
+  // BULK: thread j < eps copies edge j's whole row slice with one bulk copy
+  // that completes on the slot's mbarrier (arrival count = eps, each issuing
+  // thread arrives with the bytes it expects).  Otherwise 4-byte cp.async
+  // copies spread over the pipe.  Per-edge weights always use cp.async.
   auto issue = [&](uint32_t k) {
     if (k < nst) {
-      const int slot = (int)(k % ST_S);
+      const int slot = (int)((kg + k) % ST_S);
       const uint32_t* sid = sidx + (k % (ST_S + 1)) * eps;
       float* sb = buf + (size_t)slot * eps * swp;
-      // consecutive threads copy consecutive chunks of the same source row
-      for (int c = ptid; c < copies; c += tp) {
-        const int j = c / cpe;
-        const int q = c - j * cpe;
-        const uint32_t s = sid[j];
-        if (s == NONE) break;  // edges past the end: later c only go further
-        if (vec4)
-          cp_async16(sb + (size_t)j * swp + 4 * q, a.x + (int64_t)s * a.ld_x + f0 + 4 * q);
-        else
+      if (BULK) {
+        if (ptid < eps) {
+          const uint32_t s = sid[ptid];
+          const uint32_t mb = (uint32_t)__cvta_generic_to_shared(mbar + slot);
+          mbar_arrive_expect_tx(mb, s != NONE ? row_bytes : 0u);
+          if (s != NONE)
+            bulk_g2s(sb + (size_t)ptid * swp, a.x + (int64_t)s * a.ld_x + f0, row_bytes, mb);
+        }
+      } else {
+        const int copies = eps * fw;
+        for (int c = ptid; c < copies; c += tp) {
+          const int j = c / fw;
+          const int q = c - j * fw;
+          const uint32_t s = sid[j];
+          if (s == NONE) break;
           cp_async4(sb + (size_t)j * swp + q, a.x + (int64_t)s * a.ld_x + f0 + q);
+        }
       }
       if (ptid < eps) {
         const uint32_t s = sid[ptid];
@@ -341,6 +412,7 @@ __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint
 #pragma unroll
     for (int k = 0; k <= ST_S; k++) sidx[k * eps + ptid] = src_for((uint32_t)k);
   }
+  if (BULK) fence_proxy_async_smem();
   pipe_bar(bar_id, tp);
 #pragma unroll
   for (int k = 0; k < ST_S - 1; k++) issue((uint32_t)k);
@@ -360,13 +432,28 @@ __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint
       if (OP == OP_GCN) dinv_r = rdv[r];
     }
   };
+  bool ok = true;
   for (uint32_t k = 0; k < nst; k++) {
+    const int slot = (int)((kg + k) % ST_S);
     cp_async_wait<ST_S - 2>();
-    pipe_bar(bar_id, tp);
+    bool timed_out = false;
+    if (BULK && !mbar_wait(mbar + slot, ((kg + k) / ST_S) & 1u)) {
+      dev_raise(a.err, DEVERR_TIMEOUT, (uint64_t)rb, 3);
+      timed_out = true;
+    }
+    if (BULK) {
+      // a bounded wait ran out somewhere in the pipe: every thread leaves together
+      if (pipe_bar_or(bar_id, tp, timed_out)) {
+        ok = false;
+        break;
+      }
+    } else {
+      pipe_bar(bar_id, tp);
+    }
+    if (BULK) fence_proxy_async_smem();  // generic reads of the freed slot before async writes
     issue(k + ST_S - 1);
     const uint32_t s_ahead = src_for(k + ST_S + 1);
     if (consumer) {
-      const int slot = (int)(k % ST_S);
       const float* b = buf + (size_t)slot * eps * swp + ptid;
       const float* wb = wbuf + slot * eps;
       const uint32_t base = k * (uint32_t)eps;
@@ -404,44 +491,59 @@ __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint
         acc = step<OP>(acc, b[(size_t)j * swp], w);
       }
     }
-    // stage k+S+1's ids go to the slot stage k+S+1 - (S+1) = k used; stage k
-    // was issued two iterations ago and nobody reads that slot again
+    // stage k+S+1's ids go to the slot stage k used; stage k was issued two
+    // iterations ago and nobody reads that slot again
     if (ptid < eps) sidx[((k + ST_S + 1) % (ST_S + 1)) * eps + ptid] = s_ahead;
   }
   cp_async_wait<0>();
-  if (consumer)
-    while (r < nrows) finalize();
+  if (ok) {
+    kg += nst;
+    if (consumer)
+      while (r < nrows) finalize();
+  }
   pipe_bar(bar_id, tp);  // the ring and row buffer are reused by the next item
+  return ok;
 }
 
-template <int OP>
+template <int OP, bool BULK>
 __global__ void __launch_bounds__(ST_THREADS, 2)
-    k_agg_stream(const AggArgs a, int P, int swp, int n_slices, int vec4, uint32_t* queue) {
+    k_agg_stream(const AggArgs a, int P, int swp, int n_slices, uint32_t* queue) {
   extern __shared__ float4 st_smem4[];
   float* data = reinterpret_cast<float*>(st_smem4);
   const size_t data_f = (size_t)P * ST_S * ST_EPS * swp;
-  float* wb = data + data_f;
+  // mbarriers first after the data (8-byte aligned): heavy-mode set, then one set per pipe
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(data + data_f);
+  float* wb = reinterpret_cast<float*>(mbar + (P + 1) * ST_S);
   uint32_t* sidx = reinterpret_cast<uint32_t*>(wb + P * ST_S * ST_EPS);
   uint32_t* rps = sidx + P * (ST_S + 1) * ST_EPS;
-  uint32_t* slots = rps + P * (ST_RMAX + 1);
+  int* slots = reinterpret_cast<int*>(rps + P * (ST_RMAX + 1));  // [0..P] fetched items
   float* rdv = reinterpret_cast<float*>(slots + 16);  // present for OP_GCN only
   const int F = a.num_features;
   const uint32_t heavy_work = a.n_heavy_items * (uint32_t)n_slices;
   const uint32_t light_work = (a.n_items - a.n_heavy_items) * (uint32_t)n_slices;
+  const int tp = ST_THREADS / P;
+  if (BULK && threadIdx.x == 0) {
+    for (int i = 0; i < ST_S; i++) mbar_init(mbar + i, ST_EPS * P);  // heavy mode: 32P issuers
+    for (int p = 0; p < P; p++)
+      for (int i = 0; i < ST_S; i++) mbar_init(mbar + (p + 1) * ST_S + i, ST_EPS);
+    fence_mbar_init();
+  }
+  __syncthreads();
 
   // phase 1: heavy rows, the whole CTA as one pipe
+  uint32_t kg = 0;
   for (;;) {
-    if (threadIdx.x == 0) slots[P] = atomicAdd(&queue[0], 1u);
+    if (threadIdx.x == 0) slots[P] = (int)atomicAdd(&queue[0], 1u);
     __syncthreads();
-    const uint32_t w = slots[P];
+    const uint32_t w = (uint32_t)slots[P];
     if (w >= heavy_work) break;
     const uint2 item = a.items[w / (uint32_t)n_slices];
     const int f0 = (int)(w % (uint32_t)n_slices) * ST_SW;
-    stream_range<OP>(a, item.x, item.y, f0, min(ST_SW, F - f0), vec4, swp, ST_THREADS,
-                     threadIdx.x, ST_EPS * P, data, wb, sidx, rps, rdv, 0);
+    if (!stream_range<OP, BULK>(a, item.x, item.y, f0, min(ST_SW, F - f0), swp, ST_THREADS,
+                                threadIdx.x, ST_EPS * P, data, wb, sidx, rps, rdv, mbar, kg, 0))
+      return;
   }
   // phase 2: light items, P independent pipes
-  const int tp = ST_THREADS / P;
   const int pipe = threadIdx.x / tp, ptid = threadIdx.x % tp;
   const int bar_id = P == 1 ? 0 : pipe + 1;
   float* pdata = data + (size_t)pipe * ST_S * ST_EPS * swp;
@@ -449,35 +551,31 @@ __global__ void __launch_bounds__(ST_THREADS, 2)
   uint32_t* psidx = sidx + pipe * (ST_S + 1) * ST_EPS;
   uint32_t* prps = rps + pipe * (ST_RMAX + 1);
   float* prdv = rdv + pipe * ST_RMAX;
+  uint64_t* pmbar = mbar + (pipe + 1) * ST_S;
+  uint32_t kgp = 0;
   for (;;) {
-    if (ptid == 0) slots[pipe] = atomicAdd(&queue[1], 1u);
+    if (ptid == 0) slots[pipe] = (int)atomicAdd(&queue[1], 1u);
     pipe_bar(bar_id, tp);
-    const uint32_t w = slots[pipe];
+    const uint32_t w = (uint32_t)slots[pipe];
     if (w >= light_work) break;
     const uint2 item = a.items[a.n_heavy_items + w / (uint32_t)n_slices];
     const int f0 = (int)(w % (uint32_t)n_slices) * ST_SW;
-    stream_range<OP>(a, item.x, item.y, f0, min(ST_SW, F - f0), vec4, swp, tp, ptid, ST_EPS,
-                     pdata, pwb, psidx, prps, prdv, bar_id);
+    if (!stream_range<OP, BULK>(a, item.x, item.y, f0, min(ST_SW, F - f0), swp, tp, ptid, ST_EPS,
+                                pdata, pwb, psidx, prps, prdv, pmbar, kgp, bar_id))
+      return;
   }
 }
 
-template <int OP>
-int launch_stream(bgnn_ctx* ctx, const AggArgs& a) {
-  const int F = a.num_features;
-  const int fs = F < ST_SW ? F : ST_SW;
-  const int swp = (fs + 3) & ~3;
-  int pw = 32;
-  while (pw < swp) pw <<= 1;
-  const int P = ST_THREADS / pw;  // 1, 2, 4 or 8
-  const int n_slices = (F + ST_SW - 1) / ST_SW;
-  const bool vec4 = (F % 4 == 0) && ((uintptr_t)a.x % 16 == 0) && (a.ld_x % 4 == 0);
-  size_t smem = ((size_t)P * ST_S * ST_EPS * swp + (size_t)P * ST_S * ST_EPS) * 4 +
-                (size_t)(P * (ST_S + 1) * ST_EPS + P * (ST_RMAX + 1) + 16) * 4;
+template <int OP, bool BULK>
+int launch_stream_t(bgnn_ctx* ctx, const AggArgs& a, int P, int swp, int n_slices) {
+  size_t smem = (size_t)P * ST_S * ST_EPS * swp * 4 + (size_t)(P + 1) * ST_S * 8 +
+                ((size_t)P * ST_S * ST_EPS + (size_t)P * (ST_S + 1) * ST_EPS +
+                 (size_t)P * (ST_RMAX + 1) + 16) * 4;
   if (OP == OP_GCN) smem += (size_t)P * ST_RMAX * 4;
-  BGNN_CUDA(ctx, cudaFuncSetAttribute(k_agg_stream<OP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)smem));
+  BGNN_CUDA(ctx, cudaFuncSetAttribute(k_agg_stream<OP, BULK>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   int per_sm = 0;
-  BGNN_CUDA(ctx, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_agg_stream<OP>,
+  BGNN_CUDA(ctx, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_agg_stream<OP, BULK>,
                                                                ST_THREADS, smem));
   if (per_sm < 1) per_sm = 1;
   const uint64_t work = (uint64_t)a.n_items * n_slices;
@@ -485,10 +583,27 @@ int launch_stream(bgnn_ctx* ctx, const AggArgs& a) {
   if (grid > work) grid = work ? work : 1;
   uint32_t* queue = ctx->d_small;
   BGNN_CUDA(ctx, cudaMemsetAsync(queue, 0, 2 * sizeof(uint32_t), ctx->stream));
-  k_agg_stream<OP><<<(unsigned)grid, ST_THREADS, smem, ctx->stream>>>(a, P, swp, n_slices,
-                                                                      vec4 ? 1 : 0, queue);
+  k_agg_stream<OP, BULK><<<(unsigned)grid, ST_THREADS, smem, ctx->stream>>>(a, P, swp, n_slices,
+                                                                            queue);
   BGNN_LAUNCHED(ctx);
   return BGNN_OK;
+}
+
+template <int OP>
+int launch_stream(bgnn_ctx* ctx, const AggArgs& a0) {
+  AggArgs a = a0;
+  a.err = ctx->d_err;
+  const int F = a.num_features;
+  const int fs = F < ST_SW ? F : ST_SW;
+  const int swp = (fs + 3) & ~3;
+  int pw = 32;
+  while (pw < swp) pw <<= 1;
+  const int P = ST_THREADS / pw;  // 1, 2, 4 or 8
+  const int n_slices = (F + ST_SW - 1) / ST_SW;
+  // bulk copies need 16-byte aligned rows and sizes: F % 4 == 0 covers every slice
+  const bool bulk = (F % 4 == 0) && ((uintptr_t)a.x % 16 == 0) && (a.ld_x % 4 == 0);
+  return bulk ? launch_stream_t<OP, true>(ctx, a, P, swp, n_slices)
+              : launch_stream_t<OP, false>(ctx, a, P, swp, n_slices);
 }
 
 // ---------------------------------------------------------------------------

@@ -174,6 +174,7 @@ struct AggArgs {
   int act;
   double act_param;
   int exact;              // OP_SPMM rounding mode
+  int* err;               // device error word (set by the launcher)
 };
 int bgnn_run_aggregate(bgnn_ctx* ctx, int op, const AggArgs& a);
 

@@ -9,8 +9,10 @@
 //   BGNN_MATH_FAST:  f32 fma in the same order; differs from the reference
 //                    only where its double result lands on an f32 tie.
 // K tails are not zero-padded (an extra fma with 0 could turn a -0 into +0).
-// The SAGE variant accumulates X*W_self and Agg*W_neigh in one pass and
-// stores f32(self + neigh) (Tensor.add -> wasmAdd, sage.ts:178-183).
+// SAGE stores f32(self + neigh) (Tensor.add -> wasmAdd, sage.ts:178-183):
+// narrow outputs accumulate both products in one pass; wide outputs run the
+// 128x128 kernel twice, storing St = X*W_self as f32 (as the reference's
+// Tensor does) and adding it in the second launch's epilogue.
 #include "bgnn_internal.cuh"
 
 namespace {
@@ -143,10 +145,127 @@ __global__ void __launch_bounds__(256) k_gemm(const GemmArgs g) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// 128x128 tile, 8x8 outputs per thread (rows ty*4+{0..3} and 64+ty*4+{0..3},
+// columns tx*4+{0..3} and 64+tx*4+{0..3}): four 16-byte shared loads feed 64
+// FMAs per k step.  Optional addend matrix (SAGE: f32(St + acc)) in the
+// epilogue.  Same k-ascending order per output as wasmMatmul.
+// ---------------------------------------------------------------------------
+template <bool EXACT>
+__global__ void __launch_bounds__(256) k_sgemm128(const float* __restrict__ A,
+                                                  const float* __restrict__ B, uint32_t m,
+                                                  uint32_t k, uint32_t n,
+                                                  const float* addend,
+                                                  const float* __restrict__ bias, int act,
+                                                  double act_param, float* C, int vec) {
+  constexpr int BM = 128, BN = 128, BK = 8;
+  __shared__ __align__(16) float As[2][BK][BM];
+  __shared__ __align__(16) float Bs[2][BK][BN];
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  const uint64_t m0 = (uint64_t)blockIdx.x * BM;
+  const uint32_t n0 = blockIdx.y * BN;
+  // global load assignment: A row = tid/2, k = (tid%2)*4..+4 ; B k = tid/32, n = (tid%32)*4..+4
+  const int a_r = tid >> 1, a_k = (tid & 1) * 4;
+  const int b_k = tid >> 5, b_n = (tid & 31) * 4;
+  float ra[4], rb[4];
+  auto load = [&](uint32_t k0) {
+    const uint64_t gm = m0 + a_r;
+    if ((vec & 1) && gm < m && k0 + a_k + 3 < k) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(A + gm * k + k0 + a_k));
+      ra[0] = v.x; ra[1] = v.y; ra[2] = v.z; ra[3] = v.w;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const uint32_t gk = k0 + a_k + i;
+        ra[i] = (gm < m && gk < k) ? __ldg(A + gm * k + gk) : 0.0f;
+      }
+    }
+    const uint32_t gk = k0 + b_k;
+    if ((vec & 2) && gk < k && n0 + b_n + 3 < n) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(B + (uint64_t)gk * n + n0 + b_n));
+      rb[0] = v.x; rb[1] = v.y; rb[2] = v.z; rb[3] = v.w;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const uint32_t gn = n0 + b_n + i;
+        rb[i] = (gk < k && gn < n) ? __ldg(B + (uint64_t)gk * n + gn) : 0.0f;
+      }
+    }
+  };
+  auto store = [&](int buf) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) As[buf][a_k + i][a_r] = ra[i];
+    *reinterpret_cast<float4*>(&Bs[buf][b_k][b_n]) = make_float4(rb[0], rb[1], rb[2], rb[3]);
+  };
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; i++)
+#pragma unroll
+    for (int j = 0; j < 8; j++) acc[i][j] = 0.0f;
+
+  const uint32_t ntiles = (k + BK - 1) / BK;
+  load(0);
+  store(0);
+  __syncthreads();
+  for (uint32_t t = 0; t < ntiles; t++) {
+    const int cur = t & 1;
+    if (t + 1 < ntiles) load((t + 1) * BK);
+    const int kmax = (int)min((uint32_t)BK, k - t * BK);
+#pragma unroll
+    for (int kk = 0; kk < BK; kk++) {
+      if (kk < kmax) {
+        const float4 a0 = *reinterpret_cast<const float4*>(&As[cur][kk][ty * 4]);
+        const float4 a1 = *reinterpret_cast<const float4*>(&As[cur][kk][64 + ty * 4]);
+        const float4 b0 = *reinterpret_cast<const float4*>(&Bs[cur][kk][tx * 4]);
+        const float4 b1 = *reinterpret_cast<const float4*>(&Bs[cur][kk][64 + tx * 4]);
+        const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+#pragma unroll
+          for (int j = 0; j < 8; j++) acc[i][j] = mac<EXACT>(av[i], bv[j], acc[i][j]);
+      }
+    }
+    if (t + 1 < ntiles) store(cur ^ 1);
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    const uint64_t gm = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+    if (gm >= m) continue;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const uint32_t gn = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + (j - 4));
+      if (gn >= n) continue;
+      float v = acc[i][j];
+      if (addend) v = __fadd_rn(addend[gm * n + gn], v);
+      if (bias) v = __fadd_rn(v, bias[gn]);
+      C[gm * n + gn] = apply_act(v, act, act_param);
+    }
+  }
+}
+
 template <int BM, int BN, int TM, int TN, bool EXACT, bool DUAL>
 int launch_gemm(bgnn_ctx* ctx, const GemmArgs& g) {
   dim3 grid((unsigned)((g.m + BM - 1) / BM), (g.n + BN - 1) / BN);
   k_gemm<BM, BN, TM, TN, EXACT, DUAL><<<grid, 256, 0, ctx->stream>>>(g);
+  BGNN_LAUNCHED(ctx);
+  return BGNN_OK;
+}
+
+int launch_sgemm128(bgnn_ctx* ctx, const float* a, const float* b, uint32_t m, uint32_t k,
+                    uint32_t n, const float* addend, const float* bias, int act, double act_param,
+                    float* out, bool exact) {
+  const int vec = (((k & 3) == 0 && (uintptr_t)a % 16 == 0) ? 1 : 0) |
+                  (((n & 3) == 0 && (uintptr_t)b % 16 == 0) ? 2 : 0);
+  dim3 grid((unsigned)((m + 127) / 128), (n + 127) / 128);
+  if (exact)
+    k_sgemm128<true><<<grid, 256, 0, ctx->stream>>>(a, b, m, k, n, addend, bias, act, act_param,
+                                                    out, vec);
+  else
+    k_sgemm128<false><<<grid, 256, 0, ctx->stream>>>(a, b, m, k, n, addend, bias, act, act_param,
+                                                     out, vec);
   BGNN_LAUNCHED(ctx);
   return BGNN_OK;
 }
@@ -253,6 +372,13 @@ int bgnn_run_linear(bgnn_ctx* ctx, const float* a, const float* w, const float* 
   GemmArgs g{a, w, a2, w2, bias, out, m, k, n, act, act_param};
   const bool dual = a2 != nullptr && w2 != nullptr;
   const bool exact = ctx->math == BGNN_MATH_EXACT;
+  if (n > 64) {
+    // wide outputs: the 128x128 kernel; the SAGE pair runs as two launches,
+    // St = a2*w2 stored as f32 (the reference's Tensor), then f32(St + a*w)
+    if (dual) BGNN_TRY(launch_sgemm128(ctx, a2, w2, m, k, n, nullptr, nullptr, 0, 0.0, out, exact));
+    return launch_sgemm128(ctx, a, w, m, k, n, dual ? out : nullptr, bias, act, act_param, out,
+                           exact);
+  }
   if (exact) return dual ? pick_tile<true, true>(ctx, g) : pick_tile<true, false>(ctx, g);
   return dual ? pick_tile<false, true>(ctx, g) : pick_tile<false, false>(ctx, g);
 }

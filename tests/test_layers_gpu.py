@@ -146,9 +146,10 @@ def test_gat_softmax_overflow_regime(bg):
 
 @pytest.mark.parametrize("aggr", ["mean", "max", "sum", "pool"])
 @pytest.mark.parametrize("root", [True, False])
-def test_sage(bg, mode, aggr, root):
+@pytest.mark.parametrize("fout", [47, 130])
+def test_sage(bg, mode, aggr, root, fout):
     rng = np.random.default_rng(21)
-    n, fin, fout = 2000, 24, 47
+    n, fin = 2000, 24
     ei, e = rand_graph(n, 16000, 6, hub_deg=900, loops=3, dup=20)
     x = rng.standard_normal((n, fin)).astype(np.float32)
     wn = weights(rng, fin, fout)
