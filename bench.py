@@ -248,6 +248,140 @@ def spmm_sweep(steps, warmup, hbm_peak):
 
 
 # ---------------------------------------------------------------------------
+# the three small workloads (GCN, GAT, batched GIN): timed on the device,
+# checked against the oracle at full size, with the oracle's single-thread
+# time (the reference's one JS thread) beside them
+# ---------------------------------------------------------------------------
+def _time_device(fn, steps, warmup):
+    import torch
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        out = fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / steps, out
+
+
+def _parity(got, want):
+    g = got.astype(np.float64).ravel()
+    w = want.astype(np.float64).ravel()
+    err = np.abs(g - w)
+    bad = ~((err <= 1e-6 + 1e-5 * np.abs(w)) | (np.isnan(g) & np.isnan(w)))
+    return {"max_abs_err": float(np.nanmax(err)) if err.size else 0.0,
+            "outside_tolerance": int(bad.sum()), "elements": int(g.size),
+            "tolerance": "|gpu-ref| <= 1e-6 + 1e-5|ref|"}
+
+
+def small_workloads(steps, warmup):
+    import browsergnn_b200 as bg
+    from browsergnn_b200 import synth
+    from oracle import oracle as orc
+
+    res = {}
+    rng = np.random.default_rng(7)
+
+    # 1. 2-layer GCN 1433 -> 16 (ReLU) -> 7 on a BA graph, self-loops added
+    w = synth.gcn_cora_like()
+    n, e = w.num_nodes, w.num_edges
+    w1, b1 = synth.glorot(1433, 16, rng), rng.uniform(-0.1, 0.1, 16).astype(np.float32)
+    w2, b2 = synth.glorot(16, 7, rng), rng.uniform(-0.1, 0.1, 7).astype(np.float32)
+    l1 = bg.GCNConv(inChannels=1433, outChannels=16)
+    l1.loadStateDict({"weight": w1, "bias": b1})
+    l2 = bg.GCNConv(inChannels=16, outChannels=7)
+    l2.loadStateDict({"weight": w2, "bias": b2})
+    g = bg.GraphData(x=w.x, numNodes=n, numFeatures=1433, edgeIndex=w.edge_index, numEdges=e)
+    gd = g.withFeatures(g.x_device())
+    ms, out = _time_device(lambda: l2.forward(l1.forward(gd, _act="relu")), steps, warmup)
+    t0 = time.perf_counter()
+    h = orc.relu(orc.gcn_forward(w.x, n, 1433, w.edge_index, e, w1, b1, 16))
+    want = orc.gcn_forward(h, n, 16, w.edge_index, e, w2, b2, 7)
+    cpu_s = time.perf_counter() - t0
+    e_layer = e + (0 if g.hasSelfLoops() else n)
+    res["gcn"] = {"workload": w.name, "edges_per_layer": e_layer, "layers": 2, "ms_per_step": ms,
+                  "value": 2 * e_layer / (ms * 1e-3), "unit": UNIT,
+                  "cpu_oracle_1thread": {"value": 2 * e_layer / cpu_s, "seconds": cpu_s},
+                  "parity": _parity(out.x.cpu().numpy(), want)}
+
+    # 2. 2-layer GAT 500 -> 8 heads x 8 (ELU) -> 1 x 16 on R-MAT
+    w = synth.gat_rmat()
+    n, e = w.num_nodes, w.num_edges
+    p1 = {"weight": synth.glorot(500, 64, rng),
+          "att_src": (0.3 * rng.standard_normal((8, 8))).astype(np.float32),
+          "att_dst": (0.3 * rng.standard_normal((8, 8))).astype(np.float32),
+          "bias": rng.uniform(-0.1, 0.1, 64).astype(np.float32)}
+    p2 = {"weight": synth.glorot(64, 16, rng),
+          "att_src": (0.3 * rng.standard_normal((1, 16))).astype(np.float32),
+          "att_dst": (0.3 * rng.standard_normal((1, 16))).astype(np.float32),
+          "bias": rng.uniform(-0.1, 0.1, 16).astype(np.float32)}
+    l1 = bg.GATConv(inChannels=500, outChannels=8, heads=8)
+    l1.loadStateDict(p1)
+    l2 = bg.GATConv(inChannels=64, outChannels=16, heads=1)
+    l2.loadStateDict(p2)
+    g = bg.GraphData(x=w.x, numNodes=n, numFeatures=500, edgeIndex=w.edge_index, numEdges=e)
+    gd = g.withFeatures(g.x_device())
+    ms, out = _time_device(lambda: l2.forward(l1.forward(gd, _act="elu")), steps, warmup)
+    t0 = time.perf_counter()
+    h = orc.elu(orc.gat_forward(w.x, n, 500, w.edge_index, e, p1["weight"], p1["att_src"],
+                                p1["att_dst"], p1["bias"], 8, 8))
+    want = orc.gat_forward(h, n, 64, w.edge_index, e, p2["weight"], p2["att_src"], p2["att_dst"],
+                           p2["bias"], 1, 16)
+    cpu_s = time.perf_counter() - t0
+    e_layer = e + (0 if g.hasSelfLoops() else n)
+    res["gat"] = {"workload": w.name, "edges_per_layer": e_layer, "layers": 2, "ms_per_step": ms,
+                  "value": 2 * e_layer / (ms * 1e-3), "unit": UNIT,
+                  "cpu_oracle_1thread": {"value": 2 * e_layer / cpu_s, "seconds": cpu_s},
+                  "parity": _parity(out.x.cpu().numpy(), want)}
+
+    # 3. batched GIN: 5 layers (32 -> 64, then 64 -> 64), MLP width 64, eps 0,
+    #    ReLU between layers, global sum pool
+    w = synth.gin_batch()
+    n, e = w.num_nodes, w.num_edges
+    widths = [32, 64, 64, 64, 64, 64]
+    params, layers = [], []
+    for fin, fout in zip(widths[:-1], widths[1:]):
+        p = {"epsilon": np.zeros(1, np.float32), "mlp_weight1": synth.glorot(fin, 64, rng),
+             "mlp_bias1": rng.uniform(-0.1, 0.1, 64).astype(np.float32),
+             "mlp_weight2": synth.glorot(64, fout, rng),
+             "mlp_bias2": rng.uniform(-0.1, 0.1, fout).astype(np.float32)}
+        lay = bg.GINConv(inChannels=fin, outChannels=fout, hiddenChannels=64)
+        lay.loadStateDict(p)
+        params.append(p)
+        layers.append(lay)
+    g = bg.GraphData(x=w.x, numNodes=n, numFeatures=32, edgeIndex=w.edge_index, numEdges=e,
+                     batch=w.extra["batch"])
+    gd = g.withFeatures(g.x_device())
+    ng = w.extra["num_graphs"]
+
+    def gin_step():
+        h = gd
+        for i, lay in enumerate(layers):
+            h = lay.forward(h, _act="relu" if i < len(layers) - 1 else None)
+        return bg.global_sum_pool(h, ng)
+
+    ms, pooled = _time_device(gin_step, steps, warmup)
+    t0 = time.perf_counter()
+    h = w.x
+    for i, (p, (fin, fout)) in enumerate(zip(params, zip(widths[:-1], widths[1:]))):
+        h = orc.gin_forward(h, n, fin, w.edge_index, e, 0.0, p["mlp_weight1"], p["mlp_bias1"], 64,
+                            p["mlp_weight2"], p["mlp_bias2"], fout)
+        if i < len(layers) - 1:
+            h = orc.relu(h)
+    want = orc.sum_pool(h, n, 64, w.extra["batch"], ng)
+    cpu_s = time.perf_counter() - t0
+    res["gin"] = {"workload": w.name, "edges_per_layer": e, "layers": 5, "ms_per_step": ms,
+                  "value": 5 * e / (ms * 1e-3), "unit": UNIT,
+                  "cpu_oracle_1thread": {"value": 5 * e / cpu_s, "seconds": cpu_s},
+                  "parity": _parity(pooled.cpu().numpy(), want)}
+    return res
+
+
+# ---------------------------------------------------------------------------
 # CPU legs: the oracle restatement of the reference CPU path
 # ---------------------------------------------------------------------------
 def cpu_sample_forward(threads, frac=64, repeats=1):
@@ -274,6 +408,53 @@ def cpu_sample_forward(threads, frac=64, repeats=1):
     desc = (f"3-layer SAGE-mean forward of the CPU restatement on a 1/{frac} sample of the "
             f"workload: R-MAT {w.num_nodes} nodes / {w.num_edges} edges, same widths")
     return 3 * w.num_edges / t, desc, w.num_edges, t
+
+
+def profile_case(kind):
+    """Small, self-contained launches for ncu (profiles/ cites these):
+    small    : R-MAT 1,000,000 nodes / 25,000,000 edges, F=256: one mean
+               aggregation, then one SAGE linear 256 -> 256 (two SGEMM launches)
+    full-agg : the benchmark graph (2,450,000 / 62,000,000), F=256 mean
+               aggregation twice (capture the second)."""
+    import torch
+
+    import browsergnn_b200 as bg
+    from browsergnn_b200 import synth
+    from browsergnn_b200.backend import ptr
+    from browsergnn_b200.graph import DeviceGraph
+
+    if kind == "small":
+        scale, n, e = 20, 1_000_000, 25_000_000
+    else:
+        scale, n, e = synth.SAGE_SCALE, synth.SAGE_N, synth.SAGE_E
+    f = 256
+    bg.init_browsergnn()
+    ctx = bg.get_context()
+    ei = synth.rmat_edges_gpu(scale, n, e, synth.seed_for(4))
+    dg = DeviceGraph(ei, e, n, n)
+    gen = torch.Generator("cuda").manual_seed(1)
+    x = torch.randn((n, f), device="cuda", generator=gen)
+    agg = torch.empty((n, f), device="cuda")
+    reps = 1 if kind == "small" else 2
+    for _ in range(reps):
+        a0 = torch.cuda.Event(enable_timing=True)
+        a1 = torch.cuda.Event(enable_timing=True)
+        a0.record()
+        ctx.call("bgnn_aggregate", dg.h, 1, ptr(x), f, ptr(agg))
+        a1.record()
+        torch.cuda.synchronize()
+        print(f"aggregate mean F={f} on {n} nodes / {e} edges: {a0.elapsed_time(a1):.3f} ms")
+    if kind == "small":
+        w1 = torch.randn((f, f), device="cuda", generator=gen) * 0.05
+        w2 = torch.randn((f, f), device="cuda", generator=gen) * 0.05
+        b = torch.randn(f, device="cuda", generator=gen)
+        out = torch.empty((n, f), device="cuda")
+        a0.record()
+        ctx.call("bgnn_sage_linear", ptr(agg), ptr(x), ptr(w1), ptr(w2), n, f, f, ptr(b), 1, 0.0,
+                 ptr(out))
+        a1.record()
+        torch.cuda.synchronize()
+        print(f"sage_linear {n}x{f} -> {f}: {a0.elapsed_time(a1):.3f} ms")
 
 
 def run_reference(args, rank, world):
@@ -318,7 +499,13 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-spmm", action="store_true")
+    ap.add_argument("--no-small", action="store_true")
+    ap.add_argument("--profile", choices=["small", "full-agg"], default=None,
+                    help="run one profiling case for ncu and exit")
     args = ap.parse_args()
+    if args.profile:
+        profile_case(args.profile)
+        return
     rank = env_int("RANK", 0)
     world = env_int("WORLD_SIZE", 1)
     local = env_int("LOCAL_RANK", 0)
@@ -428,27 +615,29 @@ def main():
     if not args.no_e2e and world == 1:
         ei_host = ei.cpu().pin_memory()
         x_host = x.cpu().pin_memory()
+        res = torch.empty((n, WIDTHS[-1]), dtype=torch.float32, pin_memory=True)
         e2e_times = []
-        out_bytes = 0
         for i in range(args.warmup + args.steps):
             torch.cuda.synchronize()
             t0 = time.perf_counter()
+            # the user's call: copy the step's graph and features from pinned
+            # host memory, build GraphData (validated on the device), 3 layers,
+            # read the result back
             g = bg.GraphData(x=x_host.to("cuda", non_blocking=True), numNodes=n,
-                             numFeatures=WIDTHS[0], edgeIndex=ei_host.numpy().view(np.uint32),
+                             numFeatures=WIDTHS[0], edgeIndex=ei_host.to("cuda", non_blocking=True),
                              numEdges=e)
             out = g
             for li, lay in enumerate(layers):
                 out = lay.forward(out, _act="relu" if li < 2 else None)
-            res = out.x.cpu()
+            res.copy_(out.x)
             t1 = time.perf_counter()
-            out_bytes = res.numel() * 4
             out.device_graph().close()
             if i >= args.warmup:
                 e2e_times.append(t1 - t0)
         e2e_s = statistics.mean(e2e_times)
         e2e = {"value": 3 * e / e2e_s, "unit": UNIT,
                "h2d_bytes_per_step": int(x_host.numel() * 4 + ei_host.numel() * 4),
-               "d2h_bytes_per_step": int(out_bytes), "ms_per_step": round(1000 * e2e_s, 3),
+               "d2h_bytes_per_step": int(res.numel() * 4), "ms_per_step": round(1000 * e2e_s, 3),
                "includes": "H2D of features and edge index, device CSR build, 3 layers, D2H"}
 
     cpu = None
@@ -462,6 +651,9 @@ def main():
         del dg
         torch.cuda.empty_cache()
         spmm = spmm_sweep(max(3, args.steps // 2), 3, hbm_peak)
+    small = None
+    if not args.no_small and world == 1:
+        small = small_workloads(max(3, args.steps), 3)
 
     if rank == 0:
         line = {
@@ -481,6 +673,8 @@ def main():
             line["config"]["halo_rows_rank0"] = part.n_halo
         if spmm is not None:
             line["spmm_sweep"] = spmm
+        if small is not None:
+            line["workloads"] = small
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

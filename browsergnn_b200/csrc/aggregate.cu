@@ -15,15 +15,17 @@
 // No float atomics, no tree reductions, no FMA contraction (-fmad=false and
 // explicit _rn intrinsics).
 //
-// Two schedules:
-//   light rows  (degree < threshold): a group of G lanes per row, lanes over
-//               features (float4 when the row stride allows), U edges of
-//               row data in flight per lane.
-//   heavy rows  (degree >= threshold): one CTA per (row, 32-feature slice);
-//               256 threads stream the row's source slices into a 4-stage
-//               cp.async shared-memory ring while one warp accumulates them in
-//               edge order.  Heavy rows are sorted by degree (largest first)
-//               and run on a second stream concurrently with the light rows.
+// Schedules:
+//   streaming (k_agg_stream, the default): a persistent kernel pulls work
+//               items (each heavy row alone, largest first, then runs of light
+//               rows) from a queue; a pipe of threads streams an item's source
+//               rows into a 3-stage shared-memory ring with one bulk copy per
+//               edge and reduces them in edge order (see below).
+//   light/heavy pair (k_agg_light + k_agg_heavy): only for the appended
+//               self-loop edge of GCN/GAT loop insertion.  Light rows: a group
+//               of G lanes per row, lanes over features; heavy rows: one CTA per
+//               (row, 32-feature slice) with a cp.async ring, on a second
+//               stream concurrently with the light rows.
 #include "bgnn_internal.cuh"
 
 namespace {

@@ -152,42 +152,46 @@ __global__ void __launch_bounds__(256) k_gemm(const GemmArgs g) {
 // epilogue.  Same k-ascending order per output as wasmMatmul.
 // ---------------------------------------------------------------------------
 template <bool EXACT>
-__global__ void __launch_bounds__(256) k_sgemm128(const float* __restrict__ A,
-                                                  const float* __restrict__ B, uint32_t m,
-                                                  uint32_t k, uint32_t n,
-                                                  const float* addend,
-                                                  const float* __restrict__ bias, int act,
-                                                  double act_param, float* C, int vec) {
-  constexpr int BM = 128, BN = 128, BK = 8;
+__global__ void __launch_bounds__(256, 2) k_sgemm128(const float* __restrict__ A,
+                                                     const float* __restrict__ B, uint32_t m,
+                                                     uint32_t k, uint32_t n, const float* addend,
+                                                     const float* __restrict__ bias, int act,
+                                                     double act_param, float* C, int vec) {
+  constexpr int BM = 128, BN = 128, BK = 16;
   __shared__ __align__(16) float As[2][BK][BM];
   __shared__ __align__(16) float Bs[2][BK][BN];
   const int tid = threadIdx.x;
   const int tx = tid & 15, ty = tid >> 4;
   const uint64_t m0 = (uint64_t)blockIdx.x * BM;
   const uint32_t n0 = blockIdx.y * BN;
-  // global load assignment: A row = tid/2, k = (tid%2)*4..+4 ; B k = tid/32, n = (tid%32)*4..+4
-  const int a_r = tid >> 1, a_k = (tid & 1) * 4;
-  const int b_k = tid >> 5, b_n = (tid & 31) * 4;
-  float ra[4], rb[4];
+  // loads: A row a_r (consecutive threads, conflict-free transposed stores),
+  // k offset a_k..a_k+7;  B row b_k, columns b_n..b_n+7
+  const int a_r = tid & 127, a_k = (tid >> 7) * 8;
+  const int b_k = tid >> 4, b_n = (tid & 15) * 8;
+  const uint64_t gm_a = m0 + a_r;
+  float ra[8], rb[8];
   auto load = [&](uint32_t k0) {
-    const uint64_t gm = m0 + a_r;
-    if ((vec & 1) && gm < m && k0 + a_k + 3 < k) {
-      const float4 v = __ldg(reinterpret_cast<const float4*>(A + gm * k + k0 + a_k));
-      ra[0] = v.x; ra[1] = v.y; ra[2] = v.z; ra[3] = v.w;
+    if ((vec & 1) && gm_a < m && k0 + a_k + 7 < k) {
+      const float4* p = reinterpret_cast<const float4*>(A + gm_a * k + k0 + a_k);
+      const float4 v0 = __ldg(p), v1 = __ldg(p + 1);
+      ra[0] = v0.x; ra[1] = v0.y; ra[2] = v0.z; ra[3] = v0.w;
+      ra[4] = v1.x; ra[5] = v1.y; ra[6] = v1.z; ra[7] = v1.w;
     } else {
 #pragma unroll
-      for (int i = 0; i < 4; i++) {
+      for (int i = 0; i < 8; i++) {
         const uint32_t gk = k0 + a_k + i;
-        ra[i] = (gm < m && gk < k) ? __ldg(A + gm * k + gk) : 0.0f;
+        ra[i] = (gm_a < m && gk < k) ? __ldg(A + gm_a * k + gk) : 0.0f;
       }
     }
     const uint32_t gk = k0 + b_k;
-    if ((vec & 2) && gk < k && n0 + b_n + 3 < n) {
-      const float4 v = __ldg(reinterpret_cast<const float4*>(B + (uint64_t)gk * n + n0 + b_n));
-      rb[0] = v.x; rb[1] = v.y; rb[2] = v.z; rb[3] = v.w;
+    if ((vec & 2) && gk < k && n0 + b_n + 7 < n) {
+      const float4* p = reinterpret_cast<const float4*>(B + (uint64_t)gk * n + n0 + b_n);
+      const float4 v0 = __ldg(p), v1 = __ldg(p + 1);
+      rb[0] = v0.x; rb[1] = v0.y; rb[2] = v0.z; rb[3] = v0.w;
+      rb[4] = v1.x; rb[5] = v1.y; rb[6] = v1.z; rb[7] = v1.w;
     } else {
 #pragma unroll
-      for (int i = 0; i < 4; i++) {
+      for (int i = 0; i < 8; i++) {
         const uint32_t gn = n0 + b_n + i;
         rb[i] = (gk < k && gn < n) ? __ldg(B + (uint64_t)gk * n + gn) : 0.0f;
       }
@@ -195,40 +199,49 @@ __global__ void __launch_bounds__(256) k_sgemm128(const float* __restrict__ A,
   };
   auto store = [&](int buf) {
 #pragma unroll
-    for (int i = 0; i < 4; i++) As[buf][a_k + i][a_r] = ra[i];
+    for (int i = 0; i < 8; i++) As[buf][a_k + i][a_r] = ra[i];
     *reinterpret_cast<float4*>(&Bs[buf][b_k][b_n]) = make_float4(rb[0], rb[1], rb[2], rb[3]);
+    *reinterpret_cast<float4*>(&Bs[buf][b_k][b_n + 4]) = make_float4(rb[4], rb[5], rb[6], rb[7]);
   };
   float acc[8][8];
 #pragma unroll
   for (int i = 0; i < 8; i++)
 #pragma unroll
     for (int j = 0; j < 8; j++) acc[i][j] = 0.0f;
+  auto kstep = [&](int cur, int kk) {
+    const float4 a0 = *reinterpret_cast<const float4*>(&As[cur][kk][ty * 4]);
+    const float4 a1 = *reinterpret_cast<const float4*>(&As[cur][kk][64 + ty * 4]);
+    const float4 b0 = *reinterpret_cast<const float4*>(&Bs[cur][kk][tx * 4]);
+    const float4 b1 = *reinterpret_cast<const float4*>(&Bs[cur][kk][64 + tx * 4]);
+    const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+#pragma unroll
+      for (int j = 0; j < 8; j++) acc[i][j] = mac<EXACT>(av[i], bv[j], acc[i][j]);
+  };
 
   const uint32_t ntiles = (k + BK - 1) / BK;
-  load(0);
-  store(0);
-  __syncthreads();
-  for (uint32_t t = 0; t < ntiles; t++) {
+  if (ntiles > 0) {
+    load(0);
+    store(0);
+    __syncthreads();
+  }
+  // full tiles: no k bound checks in the inner loop
+  const uint32_t nfull = k / BK;
+  uint32_t t = 0;
+  for (; t < nfull; t++) {
     const int cur = t & 1;
     if (t + 1 < ntiles) load((t + 1) * BK);
-    const int kmax = (int)min((uint32_t)BK, k - t * BK);
 #pragma unroll
-    for (int kk = 0; kk < BK; kk++) {
-      if (kk < kmax) {
-        const float4 a0 = *reinterpret_cast<const float4*>(&As[cur][kk][ty * 4]);
-        const float4 a1 = *reinterpret_cast<const float4*>(&As[cur][kk][64 + ty * 4]);
-        const float4 b0 = *reinterpret_cast<const float4*>(&Bs[cur][kk][tx * 4]);
-        const float4 b1 = *reinterpret_cast<const float4*>(&Bs[cur][kk][64 + tx * 4]);
-        const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-        const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-#pragma unroll
-        for (int i = 0; i < 8; i++)
-#pragma unroll
-          for (int j = 0; j < 8; j++) acc[i][j] = mac<EXACT>(av[i], bv[j], acc[i][j]);
-      }
-    }
+    for (int kk = 0; kk < BK; kk++) kstep(cur, kk);
     if (t + 1 < ntiles) store(cur ^ 1);
     __syncthreads();
+  }
+  if (t < ntiles) {  // the partial last tile (never zero-padded: no extra fma steps)
+    const int cur = t & 1;
+    const int kmax = (int)(k - t * BK);
+    for (int kk = 0; kk < kmax; kk++) kstep(cur, kk);
   }
 #pragma unroll
   for (int i = 0; i < 8; i++) {

@@ -143,7 +143,7 @@ class GraphData:
             if arr.size != 2 * e:
                 raise ValueError(f"Edge index length {arr.size} doesn't match numEdges({e}) * 2")
             # graph.ts:88-92: the first out-of-range entry in flat order
-            if arr.size and (int(arr.max()) >= n or int(arr.min()) < 0):
+            if arr.size and (int(arr.max()) >= n or (arr.dtype.kind == "i" and int(arr.min()) < 0)):
                 bad = np.flatnonzero((arr >= n) | (arr < 0))
                 raise ValueError(f"Edge index {arr[bad[0]]} out of bounds for {n} nodes")
             self.edgeIndex = np.ascontiguousarray(arr, dtype=np.uint32)
