@@ -10,7 +10,13 @@ host-side mirror of the reference's API for that path:
   initBrowserGNN, getBackend, getComputeManager src/backend/index.ts
   CudaComputeManager                            (WebGPUComputeManager's method set)
   GCNConv, GATConv, SAGEConv, GINConv           src/layers/*.ts
-  ReLU, ELU, LeakyReLU, Sequential, Module      src/nn/*.ts
+  Linear, ReLU, ELU, LeakyReLU, Sigmoid, Tanh,
+  GELU, SiLU, PReLU, Softmax, LogSoftmax,
+  Dropout, Sequential, Module                   src/nn/*.ts
+  StudentMasteryPredictor,
+  LearningPathRecommender,
+  ConceptPrerequisiteMapper                     src/models/*.ts
+  serializeModel, loadModelFromJSON, ...        src/utils/serialization.ts
 """
 from ._lib import BGNNError, BGNNIndexError
 from .backend import (CudaComputeManager, get_backend, get_compute_manager, get_context,
@@ -21,6 +27,12 @@ from .layers import (ELU, GATConv, GCNConv, GINConv, LeakyReLU, Module, ReLU, SA
                      Sequential, global_sum_pool)
 from .ops import (GPUSparse, GPUTensor, MessagePassing, SparseCOO, SparseCSR, compute_gcn_norm,
                   computeGCNNorm)
+from .nn import (GELU, Dropout, Linear, LogSoftmax, PReLU, SiLU, Sigmoid, Softmax, Tanh,
+                 manual_seed)
+from .models import ConceptPrerequisiteMapper, LearningPathRecommender, StudentMasteryPredictor
+from . import serialization
+from .serialization import (deserializeModel, getModelSize, getStateDict, loadModelFromJSON,
+                            loadStateDict, saveModelToJSON, serializeModel)
 
 __all__ = [
     "BGNNError", "BGNNIndexError", "CudaComputeManager", "DeviceGraph", "ELU", "GATConv",
@@ -29,4 +41,8 @@ __all__ = [
     "batch_graphs", "computeGCNNorm", "compute_gcn_norm", "fromEdgeList", "from_edge_list",
     "getBackend", "getComputeManager", "get_backend", "get_compute_manager", "get_context",
     "global_sum_pool", "initBrowserGNN", "init_browsergnn", "isGPUAvailable", "is_gpu_available",
+    "Linear", "Sigmoid", "Tanh", "GELU", "SiLU", "PReLU", "Softmax", "LogSoftmax", "Dropout",
+    "manual_seed", "StudentMasteryPredictor", "LearningPathRecommender",
+    "ConceptPrerequisiteMapper", "serialization", "serializeModel", "deserializeModel",
+    "saveModelToJSON", "loadModelFromJSON", "getStateDict", "loadStateDict", "getModelSize",
 ]

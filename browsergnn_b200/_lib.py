@@ -17,7 +17,9 @@ OK, ERR_INVALID_ARG, ERR_OUT_OF_RANGE, ERR_CUDA, ERR_NO_MEMORY, ERR_TIMEOUT, ERR
     ERR_DEVICE = range(8)
 MATH_FAST, MATH_EXACT = 0, 1
 AGGR = {"sum": 0, "add": 0, "mean": 1, "max": 2}
-ACT = {None: 0, "none": 0, "relu": 1, "relu_max": 2, "elu": 3, "leaky_relu": 4}
+ACT = {None: 0, "none": 0, "relu": 1, "relu_max": 2, "elu": 3, "leaky_relu": 4, "sigmoid": 5,
+       "tanh": 6, "gelu": 7, "silu": 8}
+LINK = {"dot": 0, "bilinear": 1, "mlp": 2}
 
 STATUS_NAMES = {
     OK: "OK", ERR_INVALID_ARG: "INVALID_ARG", ERR_OUT_OF_RANGE: "OUT_OF_RANGE", ERR_CUDA: "CUDA",
@@ -85,6 +87,7 @@ SIGNATURES = {
     "bgnn_gcn_propagate": [_P, _P, _P, _U32, _I, _I, _P, _I, _D, _P],
     "bgnn_gat": [_P, _P, _P, _U32, _U32, _P, _P, _D, _I, _I, _P, _I, _D, _P],
     "bgnn_gat_noalloc": [_P, _P, _P, _U32, _U32, _P, _P, _D, _I, _I, _P, _I, _D, _P],
+    "bgnn_gat_train": [_P, _P, _P, _U32, _U32, _P, _P, _D, _I, _I, _P, _I, _D, _D, _U64, _P],
     "bgnn_gin_aggregate": [_P, _P, _P, _U32, _F, _P],
     "bgnn_graph_spmm": [_P, _P, _P, _P, _U32, _P],
     "bgnn_linear": [_P, _P, _P, _U32, _U32, _U32, _P, _I, _D, _P],
@@ -94,6 +97,11 @@ SIGNATURES = {
     "bgnn_pack_rows": [_P, _P, _U32, _P, _U32, _U32, _P],
     "bgnn_pool_projection": [_P, _P, _P, _P, _U32, _U32, _P],
     "bgnn_synth_rmat": [_P, _U64, _I, _U32, _U64, _D, _D, _D, _I, _P],
+    "bgnn_dense": [_P, _P, _P, _U32, _U32, _U32, _P, _I, _D, _P],
+    "bgnn_softmax_rows": [_P, _P, _U32, _U32, _P, _F, _I, _P],
+    "bgnn_dropout": [_P, _P, _U64, _D, _U64, _P],
+    "bgnn_prelu": [_P, _P, _U64, _P, _U32, _P],
+    "bgnn_link_scores": [_P, _P, _U32, _U32, _P, _P, _U64, _I, _P, _P, _P, _P, _P, _P],
 }
 _RESTYPE = {"bgnn_last_error": ctypes.c_char_p, "bgnn_ctx_launch_count": ctypes.c_uint64}
 

@@ -325,6 +325,25 @@ constexpr int ST_S = 3;       // ring stages
 constexpr int ST_EPS = 32;    // edges per stage per light pipe
 constexpr int ST_RMAX = 256;  // rows per light item (the graph's schedule builder cuts at this)
 constexpr int ST_SW = 256;    // features per slice
+constexpr int ST_GSTAGE = ST_EPS * ST_THREADS;  // floats per stage of a giant-row slice
+constexpr int ST_GSW = ST_GSTAGE / ST_THREADS;    // narrowest giant slice (ST_THREADS edges)
+
+// shared-memory regions, large enough for both the pipe layout and the
+// giant-slice layout (ST_GSTAGE floats per stage, any slice width)
+__host__ __device__ constexpr size_t stream_data_floats(int P, int swp) {
+  return (size_t)P * ST_S * ST_EPS * swp > (size_t)ST_S * ST_GSTAGE
+             ? (size_t)P * ST_S * ST_EPS * swp
+             : (size_t)ST_S * ST_GSTAGE;
+}
+__host__ __device__ constexpr size_t stream_w_floats(int P) {
+  return (size_t)P * ST_S * ST_EPS > (size_t)ST_S * ST_THREADS ? (size_t)P * ST_S * ST_EPS
+                                                                 : (size_t)ST_S * ST_THREADS;
+}
+__host__ __device__ constexpr size_t stream_sidx_words(int P) {
+  return (size_t)P * (ST_S + 1) * ST_EPS > (size_t)(ST_S + 1) * ST_THREADS
+             ? (size_t)P * (ST_S + 1) * ST_EPS
+             : (size_t)(ST_S + 1) * ST_THREADS;
+}
 
 __device__ __forceinline__ void pipe_bar(int id, int count) {
   if (id == 0)
@@ -349,7 +368,14 @@ __device__ __forceinline__ bool pipe_bar_or(int id, int count, bool pred) {
   return r != 0;
 }
 
-template <int OP, bool BULK>
+// how a stage's source rows reach shared memory
+enum : int {
+  CP_BULK = 0,  // one bulk copy (TMA engine) per edge, completing on the slot's mbarrier
+  CP_A16 = 1,   // 16-byte cp.async copies spread over the pipe (narrow rows: many per warp)
+  CP_A4 = 2,    // 4-byte cp.async copies (rows not 16-byte aligned)
+};
+
+template <int OP, int CP>
 __device__ __forceinline__ bool stream_range(const AggArgs& a, uint32_t rb, uint32_t re, int f0,
                                              int fw, int swp, int tp, int ptid, int eps,
                                              float* buf, float* wbuf, uint32_t* sidx, uint32_t* rps,
@@ -364,56 +390,69 @@ __device__ __forceinline__ bool stream_range(const AggArgs& a, uint32_t rb, uint
 
   const uint32_t nst = (ne + eps - 1) / eps;
   const uint32_t row_bytes = (uint32_t)fw * 4u;
-  constexpr uint32_t NONE = 0xffffffffu;
-  // source ids of stage k live in sidx[k % (S+1)], loaded two iterations
-  // before the stage is issued so no copy waits on an index load
-  auto src_for = [&](uint32_t k) -> uint32_t {
-    const uint32_t e = k * (uint32_t)eps + (uint32_t)ptid;
-    return (ptid < eps && k < nst && e < ne) ? a.src_of[e0 + e] : NONE;
+  // Source ids: sidx slot m % (S+1) holds stage m's ids.  Stages 0..S-2 are
+  // loaded before the ring starts; issue(m) fetches stage m+S-1's ids with
+  // cp.async in the same group as stage m's rows.  issue(m+S-1) runs at
+  // iteration m, after the wait that completes stage m's group and the
+  // barrier that publishes it, so no copy ever waits on an index load.
+  auto fetch_ids = [&](uint32_t m) {
+    const uint32_t e = m * (uint32_t)eps + (uint32_t)ptid;
+    if (ptid < eps && m < nst && e < ne)
+      cp_async4(sidx + (m % (ST_S + 1)) * eps + ptid, a.src_of + e0 + e);
   };
-  // BULK: thread j < eps copies edge j's whole row slice with one bulk copy
-  // that completes on the slot's mbarrier (arrival count = eps, each issuing
-  // thread arrives with the bytes it expects).  Otherwise 4-byte cp.async
-  // copies spread over the pipe.  Per-edge weights always use cp.async.
+  // CP_BULK: thread j < eps copies edge j's whole row slice with one bulk
+  // copy that completes on the slot's mbarrier; lane 0 of every warp of the
+  // pipe arrives for its warp with the bytes the warp's copies bring
+  // (arrival count = warps per pipe).  CP_A16 / CP_A4: cp.async copies of 16
+  // or 4 bytes spread over the pipe.  Per-edge weights always use cp.async.
   auto issue = [&](uint32_t k) {
     if (k < nst) {
       const int slot = (int)((kg + k) % ST_S);
       const uint32_t* sid = sidx + (k % (ST_S + 1)) * eps;
+      const int cnt = (int)min((uint32_t)eps, ne - k * (uint32_t)eps);  // edges in this stage
       float* sb = buf + (size_t)slot * eps * swp;
-      if (BULK) {
-        if (ptid < eps) {
-          const uint32_t s = sid[ptid];
-          const uint32_t mb = (uint32_t)__cvta_generic_to_shared(mbar + slot);
-          mbar_arrive_expect_tx(mb, s != NONE ? row_bytes : 0u);
-          if (s != NONE)
-            bulk_g2s(sb + (size_t)ptid * swp, a.x + (int64_t)s * a.ld_x + f0, row_bytes, mb);
+      if (CP == CP_BULK) {
+        const bool mine = ptid < cnt;
+        const unsigned have = __ballot_sync(0xffffffffu, mine);
+        const uint32_t mb = (uint32_t)__cvta_generic_to_shared(mbar + slot);
+        if ((ptid & 31) == 0) mbar_arrive_expect_tx(mb, (unsigned)__popc(have) * row_bytes);
+        __syncwarp();
+        if (mine)
+          bulk_g2s(sb + (size_t)ptid * swp, a.x + (int64_t)sid[ptid] * a.ld_x + f0, row_bytes, mb);
+      } else if (CP == CP_A16) {
+        const int ch = fw >> 2;  // 16-byte chunks per edge (fw is a multiple of 4 here)
+        const int copies = cnt * ch;
+        for (int c = ptid; c < copies; c += tp) {
+          const int j = c / ch;
+          const int q = c - j * ch;
+          cp_async16(sb + (size_t)j * swp + 4 * q, a.x + (int64_t)sid[j] * a.ld_x + f0 + 4 * q);
         }
       } else {
-        const int copies = eps * fw;
+        const int copies = cnt * fw;
         for (int c = ptid; c < copies; c += tp) {
           const int j = c / fw;
           const int q = c - j * fw;
-          const uint32_t s = sid[j];
-          if (s == NONE) break;
-          cp_async4(sb + (size_t)j * swp + q, a.x + (int64_t)s * a.ld_x + f0 + q);
+          cp_async4(sb + (size_t)j * swp + q, a.x + (int64_t)sid[j] * a.ld_x + f0 + q);
         }
       }
-      if (ptid < eps) {
-        const uint32_t s = sid[ptid];
-        if (s != NONE) {
-          float* w = wbuf + slot * eps + ptid;
-          if (OP == OP_GCN) cp_async4(w, a.dinv + s);
-          if (OP == OP_SPMM || OP == OP_SPMM_X) cp_async4(w, a.val + e0 + k * (uint32_t)eps + ptid);
-        }
+      if (ptid < cnt) {
+        float* w = wbuf + slot * eps + ptid;
+        if (OP == OP_GCN) cp_async4(w, a.dinv + sid[ptid]);
+        if (OP == OP_SPMM || OP == OP_SPMM_X) cp_async4(w, a.val + e0 + k * (uint32_t)eps + ptid);
       }
     }
+    fetch_ids(k + ST_S - 1);
     cp_async_commit();
   };
 
   if (ptid < eps) {
 #pragma unroll
-    for (int k = 0; k <= ST_S; k++) sidx[k * eps + ptid] = src_for((uint32_t)k);
+    for (uint32_t m = 0; m < ST_S - 1; m++) {
+      const uint32_t e = m * (uint32_t)eps + (uint32_t)ptid;
+      if (m < nst && e < ne) sidx[m * eps + ptid] = a.src_of[e0 + e];
+    }
   }
+  constexpr bool BULK = CP == CP_BULK;
   if (BULK) fence_proxy_async_smem();
   pipe_bar(bar_id, tp);
 #pragma unroll
@@ -454,7 +493,6 @@ __device__ __forceinline__ bool stream_range(const AggArgs& a, uint32_t rb, uint
     }
     if (BULK) fence_proxy_async_smem();  // generic reads of the freed slot before async writes
     issue(k + ST_S - 1);
-    const uint32_t s_ahead = src_for(k + ST_S + 1);
     if (consumer) {
       const float* b = buf + (size_t)slot * eps * swp + ptid;
       const float* wb = wbuf + slot * eps;
@@ -493,9 +531,6 @@ __device__ __forceinline__ bool stream_range(const AggArgs& a, uint32_t rb, uint
         acc = step<OP>(acc, b[(size_t)j * swp], w);
       }
     }
-    // stage k+S+1's ids go to the slot stage k used; stage k was issued two
-    // iterations ago and nobody reads that slot again
-    if (ptid < eps) sidx[((k + ST_S + 1) % (ST_S + 1)) * eps + ptid] = s_ahead;
   }
   cp_async_wait<0>();
   if (ok) {
@@ -509,41 +544,66 @@ __device__ __forceinline__ bool stream_range(const AggArgs& a, uint32_t rb, uint
 
 template <int OP, bool BULK>
 __global__ void __launch_bounds__(ST_THREADS, 2)
-    k_agg_stream(const AggArgs a, int P, int swp, int n_slices, uint32_t* queue) {
+    k_agg_stream(const AggArgs a, int P, int swp, int n_slices, uint32_t n_giant, int gsw,
+                 int eps_g, uint32_t* queue) {
   extern __shared__ float4 st_smem4[];
   float* data = reinterpret_cast<float*>(st_smem4);
-  const size_t data_f = (size_t)P * ST_S * ST_EPS * swp;
-  // mbarriers first after the data (8-byte aligned): heavy-mode set, then one set per pipe
+  const size_t data_f = stream_data_floats(P, swp);
+  // after the ring: mbarriers (heavy set, one set per pipe), then per-edge
+  // weights, source ids, row offsets, fetched items, GCN row dinv
   uint64_t* mbar = reinterpret_cast<uint64_t*>(data + data_f);
   float* wb = reinterpret_cast<float*>(mbar + (P + 1) * ST_S);
-  uint32_t* sidx = reinterpret_cast<uint32_t*>(wb + P * ST_S * ST_EPS);
-  uint32_t* rps = sidx + P * (ST_S + 1) * ST_EPS;
+  uint32_t* sidx = reinterpret_cast<uint32_t*>(wb + stream_w_floats(P));
+  uint32_t* rps = sidx + stream_sidx_words(P);
   int* slots = reinterpret_cast<int*>(rps + P * (ST_RMAX + 1));  // [0..P] fetched items
   float* rdv = reinterpret_cast<float*>(slots + 16);  // present for OP_GCN only
   const int F = a.num_features;
-  const uint32_t heavy_work = a.n_heavy_items * (uint32_t)n_slices;
+  const uint32_t gs = (uint32_t)((F + gsw - 1) / gsw);
+  const uint32_t giant_work = n_giant * gs;
+  const uint32_t heavy_work = giant_work + (a.n_heavy_items - n_giant) * (uint32_t)n_slices;
   const uint32_t light_work = (a.n_items - a.n_heavy_items) * (uint32_t)n_slices;
   const int tp = ST_THREADS / P;
-  if (BULK && threadIdx.x == 0) {
-    for (int i = 0; i < ST_S; i++) mbar_init(mbar + i, ST_EPS * P);  // heavy mode: 32P issuers
+  // heavy and light rows move by bulk copies when rows are 16-byte aligned;
+  // giant-row slices are narrow (many short rows per stage) and move by
+  // 16-byte cp.async, which spreads them over the whole CTA
+  constexpr int CP_MAIN = BULK ? CP_A16 : CP_A4;
+  constexpr int CP_GIANT = BULK ? CP_A16 : CP_A4;
+  uint64_t* mbar_heavy = mbar;
+  if (CP_MAIN == CP_BULK && threadIdx.x == 0) {
+    // one arrival per warp of the pipe and stage
+    for (int i = 0; i < ST_S; i++) mbar_init(mbar_heavy + i, ST_THREADS / 32);
     for (int p = 0; p < P; p++)
-      for (int i = 0; i < ST_S; i++) mbar_init(mbar + (p + 1) * ST_S + i, ST_EPS);
+      for (int i = 0; i < ST_S; i++) mbar_init(mbar + (p + 1) * ST_S + i, ST_THREADS / P / 32);
     fence_mbar_init();
   }
   __syncthreads();
 
-  // phase 1: heavy rows, the whole CTA as one pipe
-  uint32_t kg = 0;
+  // phase 1: heavy rows with the whole CTA as one pipe.  Giant rows (the
+  // first n_giant heavy items, chosen at launch) are cut into gsw-feature
+  // slices with eps_g edges per stage, so several CTAs stream one hub row at
+  // once; each slice is still reduced in edge order by one thread per feature.
+  uint32_t kg_heavy = 0, kg_giant = 0;  // stages run so far (ring slot and mbarrier phase)
   for (;;) {
     if (threadIdx.x == 0) slots[P] = (int)atomicAdd(&queue[0], 1u);
     __syncthreads();
     const uint32_t w = (uint32_t)slots[P];
     if (w >= heavy_work) break;
-    const uint2 item = a.items[w / (uint32_t)n_slices];
-    const int f0 = (int)(w % (uint32_t)n_slices) * ST_SW;
-    if (!stream_range<OP, BULK>(a, item.x, item.y, f0, min(ST_SW, F - f0), swp, ST_THREADS,
-                                threadIdx.x, ST_EPS * P, data, wb, sidx, rps, rdv, mbar, kg, 0))
-      return;
+    bool ok;
+    if (w < giant_work) {
+      const uint2 item = a.items[w / gs];
+      const int f0 = (int)(w % gs) * gsw;
+      ok = stream_range<OP, CP_GIANT>(a, item.x, item.y, f0, min(gsw, F - f0), gsw, ST_THREADS,
+                                      threadIdx.x, eps_g, data, wb, sidx, rps, rdv, nullptr,
+                                      kg_giant, 0);
+    } else {
+      const uint32_t w2 = w - giant_work;
+      const uint2 item = a.items[n_giant + w2 / (uint32_t)n_slices];
+      const int f0 = (int)(w2 % (uint32_t)n_slices) * ST_SW;
+      ok = stream_range<OP, CP_MAIN>(a, item.x, item.y, f0, min(ST_SW, F - f0), swp, ST_THREADS,
+                                     threadIdx.x, ST_EPS * P, data, wb, sidx, rps, rdv,
+                                     mbar_heavy, kg_heavy, 0);
+    }
+    if (!ok) return;
   }
   // phase 2: light items, P independent pipes
   const int pipe = threadIdx.x / tp, ptid = threadIdx.x % tp;
@@ -562,17 +622,16 @@ __global__ void __launch_bounds__(ST_THREADS, 2)
     if (w >= light_work) break;
     const uint2 item = a.items[a.n_heavy_items + w / (uint32_t)n_slices];
     const int f0 = (int)(w % (uint32_t)n_slices) * ST_SW;
-    if (!stream_range<OP, BULK>(a, item.x, item.y, f0, min(ST_SW, F - f0), swp, tp, ptid, ST_EPS,
-                                pdata, pwb, psidx, prps, prdv, pmbar, kgp, bar_id))
+    if (!stream_range<OP, CP_MAIN>(a, item.x, item.y, f0, min(ST_SW, F - f0), swp, tp, ptid,
+                                   ST_EPS, pdata, pwb, psidx, prps, prdv, pmbar, kgp, bar_id))
       return;
   }
 }
 
 template <int OP, bool BULK>
 int launch_stream_t(bgnn_ctx* ctx, const AggArgs& a, int P, int swp, int n_slices) {
-  size_t smem = (size_t)P * ST_S * ST_EPS * swp * 4 + (size_t)(P + 1) * ST_S * 8 +
-                ((size_t)P * ST_S * ST_EPS + (size_t)P * (ST_S + 1) * ST_EPS +
-                 (size_t)P * (ST_RMAX + 1) + 16) * 4;
+  size_t smem = stream_data_floats(P, swp) * 4 + (size_t)(P + 1) * ST_S * 8 +
+                (stream_w_floats(P) + stream_sidx_words(P) + (size_t)P * (ST_RMAX + 1) + 16) * 4;
   if (OP == OP_GCN) smem += (size_t)P * ST_RMAX * 4;
   BGNN_CUDA(ctx, cudaFuncSetAttribute(k_agg_stream<OP, BULK>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -583,10 +642,28 @@ int launch_stream_t(bgnn_ctx* ctx, const AggArgs& a, int P, int swp, int n_slice
   const uint64_t work = (uint64_t)a.n_items * n_slices;
   uint64_t grid = (uint64_t)ctx->num_sms * per_sm;
   if (grid > work) grid = work ? work : 1;
+  // Giant rows: a heavy row whose bytes exceed one CTA's fair share of the
+  // launch would finish long after the rest, so it is cut into feature slices
+  // that separate CTAs stream.  The slice is the widest power of two from 128
+  // down to ST_GSW features that keeps the largest row's slice within the
+  // share (ST_GSW at least), with ST_GSTAGE floats per stage (eps_g edges x
+  // gsw features).
+  const int F = a.num_features;
+  uint32_t n_giant = 0;
+  int gsw = ST_GSW;
+  if (a.heavy_deg != nullptr && F > ST_GSW && grid > 1) {
+    const double share = (double)a.num_edges * (double)F * 4.0 / (double)grid;
+    while (n_giant < a.n_heavy_items && (double)a.heavy_deg[n_giant] * F * 4.0 > share) n_giant++;
+    if (n_giant) {
+      gsw = 128;
+      while (gsw > ST_GSW && (gsw >= F || (double)a.heavy_deg[0] * gsw * 4.0 > share)) gsw >>= 1;
+    }
+  }
+  const int eps_g = ST_GSTAGE / gsw;  // edges per giant stage (at most ST_THREADS)
   uint32_t* queue = ctx->d_small;
   BGNN_CUDA(ctx, cudaMemsetAsync(queue, 0, 2 * sizeof(uint32_t), ctx->stream));
-  k_agg_stream<OP, BULK><<<(unsigned)grid, ST_THREADS, smem, ctx->stream>>>(a, P, swp, n_slices,
-                                                                            queue);
+  k_agg_stream<OP, BULK><<<(unsigned)grid, ST_THREADS, smem, ctx->stream>>>(
+      a, P, swp, n_slices, n_giant, gsw, eps_g, queue);
   BGNN_LAUNCHED(ctx);
   return BGNN_OK;
 }

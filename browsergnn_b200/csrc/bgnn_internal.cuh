@@ -7,6 +7,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <string>
+#include <vector>
 
 #include "bgnn.h"
 
@@ -44,6 +45,7 @@ struct bgnn_graph {
   uint2* items = nullptr;
   uint32_t n_items = 0;
   uint32_t n_heavy_items = 0;
+  std::vector<uint32_t> heavy_deg;  // degrees of the heavy items, host copy (largest first)
   int has_self_loops = 0;
   bool csr_only = false;           // built from an existing CSR (no eid/out_deg)
   float* dinv[2] = {nullptr, nullptr};  // GCN D^-1/2 without / with loop tail
@@ -164,6 +166,8 @@ struct AggArgs {
   const uint2* items;     // streaming schedule (NULL: use the light/heavy pair)
   uint32_t n_items;
   uint32_t n_heavy_items;
+  const uint32_t* heavy_deg;   // host pointer: degrees of the heavy items (launch-time split)
+  uint64_t num_edges;
   int tail;               // virtual self-loop edge after each row's edges
   int mean;               // sum * (1/count)
   int max_fix;            // -inf -> 0
@@ -183,7 +187,8 @@ int bgnn_run_aggregate(bgnn_ctx* ctx, int op, const AggArgs& a);
 // ---------------------------------------------------------------------------
 int bgnn_run_gat(bgnn_ctx* ctx, const bgnn_graph* g, const float* h, uint32_t heads, uint32_t c,
                  const float* att_src, const float* att_dst, double slope, int concat, int tail,
-                 const float* bias, int act, double act_param, float* out);
+                 const float* bias, int act, double act_param, float* out, double drop_p = 0.0,
+                 uint64_t seed = 0);
 
 // ---------------------------------------------------------------------------
 // dense (gemm.cu)
@@ -200,6 +205,17 @@ int bgnn_run_gather_rows(bgnn_ctx* ctx, const float* x, uint32_t num_x_rows,
 int bgnn_run_spmv(bgnn_ctx* ctx, const uint32_t* row_ptr, const uint32_t* col,
                   const float* val, const float* x, uint32_t num_rows, float* out);
 
+// Counter-based uniform draw in [0, 1) standing in for Math.random() at
+// position i of a training-mode dropout: the SplitMix64 output for state
+// seed + (i+1) * 0x9E3779B97F4A7C15, top 53 bits scaled by 2^-53.
+__host__ __device__ __forceinline__ double bgnn_uniform(uint64_t seed, uint64_t i) {
+  uint64_t z = seed + (i + 1) * 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  z ^= z >> 31;
+  return (double)(z >> 11) * (1.0 / 9007199254740992.0);
+}
+
 // ---------------------------------------------------------------------------
 // shared device helpers: the reference's activations and f32 store points
 // ---------------------------------------------------------------------------
@@ -213,6 +229,21 @@ __device__ __forceinline__ float apply_act(float v, int act, double p) {
       return v > 0.0f ? v : __double2float_rn(__dmul_rn(p, __dsub_rn(exp((double)v), 1.0)));
     case BGNN_ACT_LEAKY_RELU:
       return v > 0.0f ? v : __double2float_rn(__dmul_rn(p, (double)v));
+    case BGNN_ACT_SIGMOID:  // 1 / (1 + Math.exp(-x))
+      return __double2float_rn(__ddiv_rn(1.0, __dadd_rn(1.0, exp(-(double)v))));
+    case BGNN_ACT_TANH:
+      return __double2float_rn(tanh((double)v));
+    case BGNN_ACT_GELU: {  // 0.5*x*(1 + tanh(sqrt(2/pi)*(x + 0.044715*x*x*x))), left to right
+      const double x = (double)v;
+      const double s2p = __dsqrt_rn(__ddiv_rn(2.0, 3.141592653589793));
+      const double cube = __dmul_rn(__dmul_rn(__dmul_rn(0.044715, x), x), x);
+      const double inner = __dmul_rn(s2p, __dadd_rn(x, cube));
+      return __double2float_rn(__dmul_rn(__dmul_rn(0.5, x), __dadd_rn(1.0, tanh(inner))));
+    }
+    case BGNN_ACT_SILU: {  // x / (1 + Math.exp(-x))
+      const double x = (double)v;
+      return __double2float_rn(__ddiv_rn(x, __dadd_rn(1.0, exp(-x))));
+    }
     default:
       return v;
   }

@@ -47,13 +47,15 @@ AggArgs graph_args(const bgnn_graph* g, const float* x, uint32_t f, float* out) 
   a.items = g->items;
   a.n_items = g->n_items;
   a.n_heavy_items = g->n_heavy_items;
+  a.heavy_deg = g->heavy_deg.empty() ? nullptr : g->heavy_deg.data();
+  a.num_edges = g->num_edges;
   a.gin_ope = 1.0;
   a.act = BGNN_ACT_NONE;
   return a;
 }
 
 int check_act(bgnn_ctx* ctx, int act) {
-  if (act < BGNN_ACT_NONE || act > BGNN_ACT_LEAKY_RELU)
+  if (act < BGNN_ACT_NONE || act > BGNN_ACT_SILU)
     return bgnn_set_error(ctx, BGNN_ERR_INVALID_ARG, "unknown activation %d", act);
   return BGNN_OK;
 }
@@ -416,6 +418,21 @@ extern "C" int bgnn_gat(bgnn_ctx* ctx, const bgnn_graph* g, const float* h, uint
   const int tail = (add_self_loops && !g->has_self_loops) ? 1 : 0;  // gat.ts:116-118
   return bgnn_run_gat(ctx, g, h, heads, c, att_src, att_dst, negative_slope, concat, tail, bias,
                       act, act_param, out);
+}
+
+extern "C" int bgnn_gat_train(bgnn_ctx* ctx, const bgnn_graph* g, const float* h, uint32_t heads,
+                              uint32_t c, const float* att_src, const float* att_dst,
+                              double negative_slope, int concat, int add_self_loops,
+                              const float* bias, int act, double act_param, double dropout,
+                              uint64_t seed, float* out) {
+  BGNN_TRY(ctx_ok(ctx));
+  BGNN_REQUIRE(ctx, g != nullptr, "NULL graph");
+  BGNN_TRY(check_act(ctx, act));
+  BGNN_REQUIRE(ctx, h && att_src && att_dst && out, "NULL argument");
+  BGNN_REQUIRE(ctx, dropout >= 0.0 && dropout < 1.0, "attention dropout must be in [0, 1)");
+  const int tail = (add_self_loops && !g->has_self_loops) ? 1 : 0;
+  return bgnn_run_gat(ctx, g, h, heads, c, att_src, att_dst, negative_slope, concat, tail, bias,
+                      act, act_param, out, dropout, seed);
 }
 
 extern "C" int bgnn_gin_aggregate(bgnn_ctx* ctx, const bgnn_graph* g, const float* x, uint32_t f,

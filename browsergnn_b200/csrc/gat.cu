@@ -42,6 +42,10 @@ struct GatArgs {
   double slope;
   int concat, tail, act;
   double act_param;
+  // training-mode attention dropout (gat.ts:194-203): drop_p == 0 disables
+  const uint32_t* eid;  // COO edge id of each CSR slot (NULL: the slot itself)
+  double drop_p;
+  uint64_t seed;
 };
 
 __device__ __forceinline__ double shfl_d(double v, int src) {
@@ -105,6 +109,14 @@ __global__ void __launch_bounds__(GAT_WARPS * 32) k_gat(const GatArgs a) {
       const float sm = s_sum[w][hl];
       float* p = a.scratch + slot_idx * H + hl;
       if (sm > 0.0f) *p = __fdiv_rn(*p, sm);
+      if (a.drop_p > 0.0) {
+        // entry (edge e, head h) of alphaExp sits at e*heads + h in the
+        // reference, with the appended self-loops numbered after the edges
+        const uint64_t e = j < deg ? (a.eid ? (uint64_t)a.eid[b + j] : (uint64_t)b + j)
+                                   : a.num_edges + row;
+        const double u = bgnn_uniform(a.seed, e * (uint64_t)H + (uint64_t)hl);
+        *p = u < a.drop_p ? 0.0f : __double2float_rn(__ddiv_rn((double)*p, 1.0 - a.drop_p));
+      }
     }
   }
   __syncwarp();
@@ -166,7 +178,8 @@ int launch_gat(bgnn_ctx* ctx, const GatArgs& a) {
 
 int bgnn_run_gat(bgnn_ctx* ctx, const bgnn_graph* g, const float* h, uint32_t heads, uint32_t c,
                  const float* att_src, const float* att_dst, double slope, int concat, int tail,
-                 const float* bias, int act, double act_param, float* out) {
+                 const float* bias, int act, double act_param, float* out, double drop_p,
+                 uint64_t seed) {
   if (heads == 0 || c == 0)
     return bgnn_set_error(ctx, BGNN_ERR_INVALID_ARG, "heads and channels must be positive");
   if (heads > 32)
@@ -201,6 +214,9 @@ int bgnn_run_gat(bgnn_ctx* ctx, const bgnn_graph* g, const float* h, uint32_t he
   a.tail = tail;
   a.act = act;
   a.act_param = act_param;
+  a.eid = g->eid;
+  a.drop_p = drop_p;
+  a.seed = seed;
   const int ko = (int)((od + 31) / 32);
   if (ko <= 1) return launch_gat<1>(ctx, a);
   if (ko <= 2) return launch_gat<2>(ctx, a);
@@ -262,7 +278,7 @@ extern "C" int bgnn_gat_noalloc(bgnn_ctx* ctx, const bgnn_graph* g, const float*
   BGNN_CUDA(ctx, cudaSetDevice(ctx->device));
   BGNN_REQUIRE(ctx, g != nullptr, "NULL graph");
   BGNN_REQUIRE(ctx, h && att_src && att_dst && out, "NULL argument");
-  BGNN_REQUIRE(ctx, act >= BGNN_ACT_NONE && act <= BGNN_ACT_LEAKY_RELU, "unknown activation %d", act);
+  BGNN_REQUIRE(ctx, act >= BGNN_ACT_NONE && act <= BGNN_ACT_SILU, "unknown activation %d", act);
   BGNN_REQUIRE(ctx, heads > 0 && c > 0, "heads and channels must be positive");
   if (heads > 32)
     return bgnn_set_error(ctx, BGNN_ERR_UNSUPPORTED, "GAT supports up to 32 heads (got %u)", heads);
@@ -301,6 +317,9 @@ extern "C" int bgnn_gat_noalloc(bgnn_ctx* ctx, const bgnn_graph* g, const float*
   a.tail = tail;
   a.act = act;
   a.act_param = act_param;
+  a.eid = g->eid;
+  a.drop_p = 0.0;
+  a.seed = 0;
   const int ko = (int)((od + 31) / 32);
   if (ko <= 1) return launch_gat<1>(ctx, a);
   if (ko <= 2) return launch_gat<2>(ctx, a);

@@ -129,6 +129,7 @@ int build_schedule(bgnn_ctx* ctx, bgnn_graph* g) {
   g->n_heavy = 0;
   g->n_items = 0;
   g->n_heavy_items = 0;
+  g->heavy_deg.clear();
   const uint32_t n = g->n_dst;
   if (n == 0) return BGNN_OK;
   std::vector<uint32_t> rp((size_t)n + 1);
@@ -177,6 +178,8 @@ int build_schedule(bgnn_ctx* ctx, bgnn_graph* g) {
                             cudaMemcpyHostToDevice));
   g->n_items = (uint32_t)items.size();
   g->n_heavy_items = (uint32_t)heavy.size();
+  g->heavy_deg.resize(heavy.size());
+  for (size_t i = 0; i < heavy.size(); i++) g->heavy_deg[i] = rp[heavy[i] + 1] - rp[heavy[i]];
   return BGNN_OK;
 }
 

@@ -22,6 +22,18 @@ from .backend import get_context, ptr
 from .graph import GraphData
 
 _rng = np.random.default_rng(0xB200)
+_seed_rng = np.random.default_rng(0xB2000D)
+
+
+def manual_seed(seed: int) -> None:
+    """Reseed the generator that gives each training-mode dropout call
+    (Dropout modules, GAT attention dropout) its own seed."""
+    global _seed_rng
+    _seed_rng = np.random.default_rng(int(seed))
+
+
+def next_dropout_seed() -> int:
+    return int(_seed_rng.integers(0, 2 ** 63, dtype=np.int64))
 
 
 def _torch():
@@ -232,20 +244,23 @@ class GATConv(Module):
     def outputDim(self) -> int:
         return self.heads * self.outChannels if self.concat else self.outChannels
 
-    def forward(self, input: GraphData, _act=None) -> GraphData:
+    def forward(self, input: GraphData, _act=None, seed: Optional[int] = None) -> GraphData:
         torch = _torch()
-        if self._training and self.dropout > 0:
-            # gat.ts:195-203 draws Math.random per attention weight; the
-            # inference backend does not reproduce random training dropout
-            raise NotImplementedError("GATConv attention dropout is training-only; call eval()")
         dg, x = _prepare(self, input, self.inChannels, "GATConv")
         ctx = dg.ctx
         h = _linear(ctx, x, self.p("weight"))  # H = X @ W  (gat.ts:130)
         out = torch.empty((input.numNodes, self.outputDim), dtype=torch.float32, device=x.device)
         code, param = _act_code(_act)
-        ctx.call("bgnn_gat", dg.h, ptr(h), self.heads, self.outChannels, ptr(self.p("att_src")),
-                 ptr(self.p("att_dst")), self.negativeSlope, int(self.concat),
-                 int(self.addSelfLoops), ptr(self.p("bias")), code, param, ptr(out))
+        args = (dg.h, ptr(h), self.heads, self.outChannels, ptr(self.p("att_src")),
+                ptr(self.p("att_dst")), self.negativeSlope, int(self.concat),
+                int(self.addSelfLoops), ptr(self.p("bias")), code, param)
+        if self._training and self.dropout > 0:
+            # gat.ts:194-203: attention dropout while training, one draw per
+            # (edge, head) from the counter-based generator
+            s = next_dropout_seed() if seed is None else int(seed)
+            ctx.call("bgnn_gat_train", *args, self.dropout, s, ptr(out))
+        else:
+            ctx.call("bgnn_gat", *args, ptr(out))
         return input.withFeatures(out)
 
     forwardAsync = forward
@@ -394,14 +409,39 @@ class LeakyReLU(_Act):
         self.param = float(negativeSlope)
 
 
+_FUSABLE = [GCNConv, GATConv, SAGEConv, GINConv]
+
+
+def register_fusable(cls):
+    """Mark a module whose forward(x, _act=(name, param)) applies an
+    elementwise activation in its own epilogue."""
+    if cls not in _FUSABLE:
+        _FUSABLE.append(cls)
+    return cls
+
+
 class Sequential(Module):
-    """src/nn/module.ts:144-178.  A conv layer followed by an activation module
-    runs the activation in the layer's epilogue (same operations, one pass)."""
+    """src/nn/module.ts:144-178.  A layer (conv or Linear) followed by an
+    elementwise activation module runs the activation in the layer's epilogue
+    (same operations on the same stored values, one pass).  Takes the modules
+    as a list (the reference's form) or as separate arguments."""
 
     def __init__(self, *modules):
         super().__init__()
+        if len(modules) == 1 and isinstance(modules[0], (list, tuple)):
+            modules = tuple(modules[0])
         for i, m in enumerate(modules):
             self.registerModule(str(i), m)
+
+    def add(self, module):
+        self.registerModule(str(len(self._modules)), module)
+
+    @property
+    def length(self) -> int:
+        return len(self._modules)
+
+    def __len__(self):
+        return len(self._modules)
 
     def forward(self, input):
         mods = list(self._modules.values())
@@ -410,7 +450,7 @@ class Sequential(Module):
         while i < len(mods):
             m = mods[i]
             nxt = mods[i + 1] if i + 1 < len(mods) else None
-            if isinstance(m, (GCNConv, GATConv, SAGEConv, GINConv)) and isinstance(nxt, _Act):
+            if isinstance(m, tuple(_FUSABLE)) and isinstance(nxt, _Act):
                 x = m.forward(x, _act=(nxt.act, nxt.param))
                 i += 2
             else:

@@ -73,8 +73,19 @@ typedef enum bgnn_act {
   BGNN_ACT_RELU = 1,       /* wasmRelu: x > 0 ? x : 0   (index.ts:250-271)  */
   BGNN_ACT_RELU_MAX = 2,   /* Math.max(0, x): NaN kept  (gin.ts:106-112)    */
   BGNN_ACT_ELU = 3,        /* x > 0 ? x : a*(exp(x)-1)  (activation.ts:56-65) */
-  BGNN_ACT_LEAKY_RELU = 4  /* x > 0 ? x : s*x           (tensor.ts:401-408) */
+  BGNN_ACT_LEAKY_RELU = 4, /* x > 0 ? x : s*x           (tensor.ts:401-408) */
+  BGNN_ACT_SIGMOID = 5,    /* 1/(1+exp(-x)) in f64      (tensor.ts:413-419) */
+  BGNN_ACT_TANH = 6,       /* Math.tanh(x)              (tensor.ts:424-430) */
+  BGNN_ACT_GELU = 7,       /* tanh-form GELU in f64     (activation.ts:129-147) */
+  BGNN_ACT_SILU = 8        /* x/(1+exp(-x)) in f64      (activation.ts:153-168) */
 } bgnn_act;
+
+/* link scorers of ConceptPrerequisiteMapper (ConceptPrerequisiteMapper.ts:224-295) */
+typedef enum bgnn_link_mode {
+  BGNN_LINK_DOT = 0,      /* sigmoid(sum_i s[i]*t[i])                 */
+  BGNN_LINK_BILINEAR = 1, /* sigmoid(sum_i s[i]*f32(W t)[i])          */
+  BGNN_LINK_MLP = 2       /* sigmoid(Linear(ReLU(Linear([s,t,s*t]))))   */
+} bgnn_link_mode;
 
 typedef struct bgnn_ctx bgnn_ctx;
 typedef struct bgnn_graph bgnn_graph;
@@ -202,6 +213,17 @@ BGNN_API int bgnn_gcn_propagate(bgnn_ctx* ctx, const bgnn_graph* g, const float*
 BGNN_API int bgnn_gat(bgnn_ctx* ctx, const bgnn_graph* g, const float* h, uint32_t heads, uint32_t c,
              const float* att_src, const float* att_dst, double negative_slope, int concat,
              int add_self_loops, const float* bias, int act, double act_param, float* out);
+/* GATConv.forward in training mode (gat.ts:107-258 with :194-203): bgnn_gat
+ * plus attention dropout.  Entry (edge e, head h) of the normalised attention
+ * (e counts the appended self-loops after the edges) is zeroed when u < p and
+ * otherwise divided by (1 - p) in double, with u = the counter-based draw of
+ * bgnn_dropout at position e*heads + h standing in for Math.random().
+ * dropout in [0, 1). */
+BGNN_API int bgnn_gat_train(bgnn_ctx* ctx, const bgnn_graph* g, const float* h, uint32_t heads,
+                            uint32_t c, const float* att_src, const float* att_dst,
+                            double negative_slope, int concat, int add_self_loops,
+                            const float* bias, int act, double act_param, double dropout,
+                            uint64_t seed, float* out);
 /* bgnn_gat without any device allocation (no counterpart in the reference).
  * For callers that must not allocate once running -- an inference server
  * that reserves its memory budget at start-up, or a host application (such as
@@ -260,6 +282,45 @@ BGNN_API int bgnn_pack_rows(bgnn_ctx* ctx, const float* x, uint32_t num_x_rows, 
 BGNN_API int bgnn_synth_rmat(bgnn_ctx* ctx, uint64_t seed, int scale, uint32_t num_nodes,
                              uint64_t num_edges, double a, double b, double c, int permute,
                              uint32_t* edge_index);
+
+/* ---- model zoo building blocks (src/nn/, src/core/tensor.ts, src/models/) ----
+ * Device pointers, asynchronous on the context stream; index errors surface
+ * at the next synchronising call (bgnn_ctx_synchronize or a *_host call). */
+
+/* Linear.forward (src/nn/linear.ts:50-111): out[m, n] = act(f32(f32(x w^T) + b))
+ * where the sum over k is one double per output, ascending, w is
+ * [n, k] ([outFeatures, inFeatures]) and bias may be NULL.  act applies the
+ * activation module that follows in a Sequential. */
+BGNN_API int bgnn_dense(bgnn_ctx* ctx, const float* x, const float* w, uint32_t m, uint32_t k,
+                        uint32_t n, const float* bias, int act, double act_param, float* out);
+/* Tensor.softmax (log_softmax = 0) / Tensor.logSoftmax (1) along the rows of
+ * [rows, cols] (src/core/tensor.ts:435-499).  col_mask may be NULL; where
+ * col_mask[c] != 0 the input reads mask_value (LearningPathRecommender.ts:
+ * 190-203 masks mastered concepts with -1e9 before its softmax). */
+BGNN_API int bgnn_softmax_rows(bgnn_ctx* ctx, const float* x, uint32_t rows, uint32_t cols,
+                               const uint8_t* col_mask, float mask_value, int log_softmax,
+                               float* out);
+/* Dropout.forward in training mode (src/nn/activation.ts:207-245): keeps
+ * element i when u_i > p and scales it by 1/(1-p).  u_i is a counter-based
+ * draw in [0, 1) (SplitMix64 of seed + (i+1)*0x9E3779B97F4A7C15, top 53 bits)
+ * standing in for Math.random(); in eval mode Dropout is the identity and
+ * needs no call.  p outside [0, 1] -> BGNN_ERR_INVALID_ARG. */
+BGNN_API int bgnn_dropout(bgnn_ctx* ctx, const float* x, uint64_t n, double p, uint64_t seed,
+                          float* out);
+/* PReLU (src/nn/activation.ts:175-200): x > 0 ? x : a*x, a = weight[0] when
+ * num_params == 1, else weight[i % num_params]. */
+BGNN_API int bgnn_prelu(bgnn_ctx* ctx, const float* x, uint64_t n, const float* weight,
+                        uint32_t num_params, float* out);
+/* ConceptPrerequisiteMapper.predictLinks (ConceptPrerequisiteMapper.ts:224-295):
+ * out[q] (double) scores the pair (src[q], tgt[q]) of rows of emb
+ * [num_nodes, dim].  mode: bgnn_link_mode.  bilinear: w_bilinear [dim, dim];
+ * mlp: w1 [dim, 3*dim], b1 [dim] (or NULL), w2 [1, dim], b2 [1] (or NULL),
+ * the eval-mode network (its Dropout is the identity).  dim <= 1600 for mlp.
+ * An out-of-range node id is reported as BGNN_ERR_OUT_OF_RANGE. */
+BGNN_API int bgnn_link_scores(bgnn_ctx* ctx, const float* emb, uint32_t num_nodes, uint32_t dim,
+                              const uint32_t* src, const uint32_t* tgt, uint64_t num_pairs,
+                              int mode, const float* w_bilinear, const float* w1, const float* b1,
+                              const float* w2, const float* b2, double* out);
 
 #ifdef __cplusplus
 }

@@ -354,6 +354,17 @@ int orc_gat_forward(const float* x, int64_t n, int64_t fin, const uint32_t* ei, 
                     const float* weight, const float* att_src, const float* att_dst,
                     const float* bias, int64_t heads, int64_t c, double slope, int concat,
                     int add_self_loops, float* out) {
+  return orc_gat_forward_train(x, n, fin, ei, e, weight, att_src, att_dst, bias, heads, c, slope,
+                               concat, add_self_loops, 0.0, 0, out);
+}
+
+/* GATConv.forward in training mode: the attention dropout of gat.ts:194-203
+ * applied to alphaExp in index order, Math.random() replaced by the
+ * counter-based draw orc_uniform(seed, i). */
+int orc_gat_forward_train(const float* x, int64_t n, int64_t fin, const uint32_t* ei, int64_t e,
+                          const float* weight, const float* att_src, const float* att_dst,
+                          const float* bias, int64_t heads, int64_t c, double slope, int concat,
+                          int add_self_loops, double drop_p, uint64_t seed, float* out) {
   int64_t ep;
   uint32_t* pe = maybe_self_loops(ei, e, n, add_self_loops, &ep);
   const int64_t hc = heads * c;
@@ -400,6 +411,11 @@ int orc_gat_forward(const float* x, int64_t n, int64_t fin, const uint32_t* ei, 
         aexp[i * heads + hh] = (float)((double)aexp[i * heads + hh] / (double)sm);
     }
   }
+  if (drop_p > 0.0)
+    for (int64_t i = 0; i < ep * heads; i++)
+      aexp[i] = orc_uniform(seed, (uint64_t)i) < drop_p
+                    ? 0.0f
+                    : (float)((double)aexp[i] / (1.0 - drop_p));
   /* weighted aggregation, :209-243 */
   const int64_t od = concat ? hc : c;
   memset(out, 0, sizeof(float) * (size_t)(n * od));
@@ -642,4 +658,150 @@ int orc_sage_forward_csr(const uint32_t* row_ptr, const uint32_t* src_of, int64_
     }
   free(agg); free(nt);
   return 0;
+}
+
+/* ======================================================================= */
+/* model zoo                                                               */
+/* ======================================================================= */
+
+/* Linear.forward, src/nn/linear.ts:50-111 (the 2-D branch; the 1-D branch is
+ * the same sum for one row): `let sum = 0; sum += x*w` in double, stored to a
+ * Float32Array, then the bias loop adds b[j] in double and stores again. */
+void orc_linear(const float* x, int64_t m, int64_t k, const float* w, const float* b, int64_t n,
+                float* out) {
+  for (int64_t r = 0; r < m; r++) {
+    for (int64_t j = 0; j < n; j++) {
+      double sum = 0.0;
+      for (int64_t i = 0; i < k; i++) sum += (double)x[r * k + i] * (double)w[j * k + i];
+      float y = (float)sum;
+      if (b) y = (float)((double)y + (double)b[j]);
+      out[r * n + j] = y;
+    }
+  }
+}
+
+/* Tensor.sigmoid, src/core/tensor.ts:413-419: 1 / (1 + Math.exp(-x)). */
+void orc_sigmoid(const float* x, int64_t n, float* out) {
+  for (int64_t i = 0; i < n; i++) out[i] = (float)(1.0 / (1.0 + exp(-(double)x[i])));
+}
+
+/* Tensor.tanh, src/core/tensor.ts:424-430. */
+void orc_tanh(const float* x, int64_t n, float* out) {
+  for (int64_t i = 0; i < n; i++) out[i] = (float)tanh((double)x[i]);
+}
+
+/* GELU (tanh form), src/nn/activation.ts:129-147, left-to-right in double. */
+void orc_gelu(const float* x, int64_t n, float* out) {
+  const double s2p = sqrt(2.0 / 3.141592653589793);
+  for (int64_t i = 0; i < n; i++) {
+    const double v = (double)x[i];
+    const double inner = s2p * (v + 0.044715 * v * v * v);
+    out[i] = (float)(0.5 * v * (1.0 + tanh(inner)));
+  }
+}
+
+/* SiLU, src/nn/activation.ts:153-168: x / (1 + Math.exp(-x)). */
+void orc_silu(const float* x, int64_t n, float* out) {
+  for (int64_t i = 0; i < n; i++) {
+    const double v = (double)x[i];
+    out[i] = (float)(v / (1.0 + exp(-v)));
+  }
+}
+
+/* PReLU, src/nn/activation.ts:175-200: one slope, or slope i % numParams. */
+void orc_prelu(const float* x, int64_t n, const float* w, int64_t nw, float* out) {
+  for (int64_t i = 0; i < n; i++) {
+    const double v = (double)x[i];
+    const double a = (double)(nw == 1 ? w[0] : w[i % nw]);
+    out[i] = v > 0.0 ? (float)v : (float)(a * v);
+  }
+}
+
+/* Math.max: NaN if either is NaN; +0 beats -0. */
+static inline double js_max(double a, double b) {
+  if (a != a || b != b) return NAN;
+  if (a == 0.0 && b == 0.0) return signbit(a) ? b : a;
+  return a > b ? a : b;
+}
+
+/* Tensor.softmax / logSoftmax, src/core/tensor.ts:435-499.  softmax stores
+ * f32(exp) first and divides the stored value by the double sum of the
+ * unrounded exps; logSoftmax subtracts max + log(sum) from x. */
+void orc_softmax_rows(const float* x, int64_t rows, int64_t cols, const uint8_t* col_mask,
+                      float mask_value, int log_softmax, float* out) {
+  for (int64_t r = 0; r < rows; r++) {
+    const float* xr = x + r * cols;
+    float* o = out + r * cols;
+#define XV(c) ((col_mask && col_mask[c]) ? (double)mask_value : (double)xr[c])
+    double mx = -INFINITY;
+    for (int64_t c = 0; c < cols; c++) mx = js_max(mx, XV(c));
+    double sum = 0.0;
+    if (log_softmax) {
+      for (int64_t c = 0; c < cols; c++) sum += exp(XV(c) - mx);
+      const double lse = mx + log(sum);
+      for (int64_t c = 0; c < cols; c++) o[c] = (float)(XV(c) - lse);
+    } else {
+      for (int64_t c = 0; c < cols; c++) {
+        const double e = exp(XV(c) - mx);
+        o[c] = (float)e;
+        sum += e;
+      }
+      for (int64_t c = 0; c < cols; c++) o[c] = (float)((double)o[c] / sum);
+    }
+#undef XV
+  }
+}
+
+double orc_uniform(uint64_t seed, uint64_t i) {
+  uint64_t z = seed + (i + 1) * 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  z ^= z >> 31;
+  return (double)(z >> 11) * (1.0 / 9007199254740992.0);
+}
+
+void orc_dropout(const float* x, int64_t n, double p, uint64_t seed, float* out) {
+  const double scale = 1.0 / (1.0 - p);
+  for (int64_t i = 0; i < n; i++)
+    out[i] = orc_uniform(seed, (uint64_t)i) > p ? (float)((double)x[i] * scale) : 0.0f;
+}
+
+/* ConceptPrerequisiteMapper.predictLinks, ConceptPrerequisiteMapper.ts:224-295.
+ * The embeddings are copied into Float32Arrays (no rounding); dot and
+ * bilinear sums are JS doubles, the bilinear W*tgt vector is stored to a
+ * Float32Array, the mlp input holds f32(src*tgt) in its last third. */
+void orc_link_scores(const float* emb, int64_t d, const uint32_t* src, const uint32_t* tgt,
+                     int64_t num_pairs, int mode, const float* w_bilinear, const float* w1,
+                     const float* b1, const float* w2, const float* b2, double* out) {
+  float* tmp = (float*)malloc(sizeof(float) * (size_t)(4 * d + 1));
+  for (int64_t q = 0; q < num_pairs; q++) {
+    const float* s = emb + (int64_t)src[q] * d;
+    const float* t = emb + (int64_t)tgt[q] * d;
+    double score = 0.0;
+    if (mode == 0) {
+      for (int64_t i = 0; i < d; i++) score += (double)s[i] * (double)t[i];
+    } else if (mode == 1) {
+      for (int64_t i = 0; i < d; i++) {
+        double sum = 0.0;
+        for (int64_t j = 0; j < d; j++) sum += (double)w_bilinear[i * d + j] * (double)t[j];
+        tmp[i] = (float)sum;
+      }
+      for (int64_t i = 0; i < d; i++) score += (double)s[i] * (double)tmp[i];
+    } else {
+      float* in = tmp;          /* [3d] */
+      float* hid = tmp + 3 * d; /* [d]  */
+      for (int64_t i = 0; i < d; i++) {
+        in[i] = s[i];
+        in[d + i] = t[i];
+        in[2 * d + i] = (float)((double)s[i] * (double)t[i]);
+      }
+      orc_linear(in, 1, 3 * d, w1, b1, d, hid);
+      orc_relu(hid, d, hid);
+      float o;
+      orc_linear(hid, 1, d, w2, b2, 1, &o);
+      score = (double)o;
+    }
+    out[q] = 1.0 / (1.0 + exp(-score));
+  }
+  free(tmp);
 }

@@ -79,6 +79,12 @@ int orc_gat_forward(const float* x, int64_t n, int64_t fin, const uint32_t* edge
                     int64_t num_edges, const float* weight, const float* att_src,
                     const float* att_dst, const float* bias, int64_t heads, int64_t c,
                     double negative_slope, int concat, int add_self_loops, float* out);
+/* training mode: attention dropout p with the counter-based draw (seed) */
+int orc_gat_forward_train(const float* x, int64_t n, int64_t fin, const uint32_t* edge_index,
+                          int64_t num_edges, const float* weight, const float* att_src,
+                          const float* att_dst, const float* bias, int64_t heads, int64_t c,
+                          double negative_slope, int concat, int add_self_loops, double drop_p,
+                          uint64_t seed, float* out);
 /* aggr: 0 mean, 1 max, 2 sum, 3 pool.  lin_self NULL => rootWeight=false. */
 int orc_sage_forward(const float* x, int64_t n, int64_t fin, const uint32_t* edge_index,
                      int64_t num_edges, int aggr, const float* lin_neighbor,
@@ -111,6 +117,38 @@ int orc_sage_forward_csr(const uint32_t* row_ptr, const uint32_t* src_of, int64_
                          int relu, int threads, float* out);
 void orc_matmul_par(const float* a, const float* b, int64_t m, int64_t k, int64_t n,
                     int threads, float* out);
+
+/* ---- model zoo: src/nn/linear.ts, src/nn/activation.ts, src/core/tensor.ts,
+ *      and the three models under src/models/ ------------------------------ */
+/* Linear.forward (src/nn/linear.ts:50-111): y[r,j] = f32(sum_i x[r,i]*w[j,i])
+ * with the sum in double over i ascending, then f32(y + b[j]).  w is
+ * [n, k] ([outFeatures, inFeatures]); b may be NULL. */
+void orc_linear(const float* x, int64_t m, int64_t k, const float* w, const float* b, int64_t n,
+                float* out);
+void orc_sigmoid(const float* x, int64_t n, float* out); /* tensor.ts:413-419 */
+void orc_tanh(const float* x, int64_t n, float* out);    /* tensor.ts:424-430 */
+void orc_gelu(const float* x, int64_t n, float* out);    /* activation.ts:129-147 */
+void orc_silu(const float* x, int64_t n, float* out);    /* activation.ts:153-168 */
+void orc_prelu(const float* x, int64_t n, const float* w, int64_t nw, float* out); /* :175-200 */
+/* Tensor.softmax / logSoftmax along the last axis (tensor.ts:435-499).
+ * col_mask (may be NULL): column c with col_mask[c] != 0 reads mask_value
+ * instead of x (the -1e9 mastery mask of LearningPathRecommender.ts:190-203). */
+void orc_softmax_rows(const float* x, int64_t rows, int64_t cols, const uint8_t* col_mask,
+                      float mask_value, int log_softmax, float* out);
+/* The uniform draw that stands in for Math.random() at element i: the
+ * SplitMix64 output of state seed + (i+1)*0x9E3779B97F4A7C15, top 53 bits
+ * scaled to [0, 1). */
+double orc_uniform(uint64_t seed, uint64_t i);
+/* Dropout.forward in training mode (activation.ts:207-245): keep element i
+ * when u_i > p and scale it by 1/(1-p) in double; else 0. */
+void orc_dropout(const float* x, int64_t n, double p, uint64_t seed, float* out);
+/* ConceptPrerequisiteMapper.predictLinks (ConceptPrerequisiteMapper.ts:224-295)
+ * for pairs (src[q], tgt[q]) of node embeddings emb [num_nodes, d]; scores in
+ * double.  mode 0 dot, 1 bilinear (w_bilinear [d, d]), 2 mlp (w1 [d, 3d],
+ * b1 [d], w2 [1, d], b2 [1]; Dropout between them is the identity in eval). */
+void orc_link_scores(const float* emb, int64_t d, const uint32_t* src, const uint32_t* tgt,
+                     int64_t num_pairs, int mode, const float* w_bilinear, const float* w1,
+                     const float* b1, const float* w2, const float* b2, double* out);
 
 #ifdef __cplusplus
 }

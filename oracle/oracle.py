@@ -81,6 +81,22 @@ def _declare(L):
                                   ctypes.c_int, _F]),
         "orc_sage_forward_csr": (ctypes.c_int, [_U, _U, _I64, _F, _I64, ctypes.c_int, _F, _F,
                                                 _F, _I64, ctypes.c_int, ctypes.c_int, _F]),
+        "orc_linear": (v, [_F, _I64, _I64, _F, _F, _I64, _F]),
+        "orc_gat_forward_train": (ctypes.c_int, [_F, _I64, _I64, _U, _I64, _F, _F, _F, _F, _I64,
+                                                 _I64, ctypes.c_double, ctypes.c_int,
+                                                 ctypes.c_int, ctypes.c_double, ctypes.c_uint64,
+                                                 _F]),
+        "orc_sigmoid": (v, [_F, _I64, _F]),
+        "orc_tanh": (v, [_F, _I64, _F]),
+        "orc_gelu": (v, [_F, _I64, _F]),
+        "orc_silu": (v, [_F, _I64, _F]),
+        "orc_prelu": (v, [_F, _I64, _F, _I64, _F]),
+        "orc_softmax_rows": (v, [_F, _I64, _I64, ctypes.POINTER(ctypes.c_uint8), ctypes.c_float,
+                                 ctypes.c_int, _F]),
+        "orc_uniform": (ctypes.c_double, [ctypes.c_uint64, ctypes.c_uint64]),
+        "orc_dropout": (v, [_F, _I64, ctypes.c_double, ctypes.c_uint64, _F]),
+        "orc_link_scores": (v, [_F, _I64, _U, _U, _I64, ctypes.c_int, _F, _F, _F, _F, _F,
+                                ctypes.POINTER(ctypes.c_double)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -264,13 +280,14 @@ def gcn_forward(x, n, fin, edge_index, num_edges, weight, bias, fout, add_self_l
 
 
 def gat_forward(x, n, fin, edge_index, num_edges, weight, att_src, att_dst, bias, heads, c,
-                negative_slope=0.2, concat=True, add_self_loops=True):
+                negative_slope=0.2, concat=True, add_self_loops=True, dropout=0.0, seed=0):
     od = heads * c if concat else c
     out = np.empty(n * od, np.float32)
-    rc = lib().orc_gat_forward(_pf(_f(x)), n, fin, _pu(_u(edge_index)), num_edges,
-                               _pf(_f(weight)), _pf(_f(att_src)), _pf(_f(att_dst)),
-                               _pf(_f(bias)), heads, c, float(negative_slope), int(concat),
-                               int(add_self_loops), _pf(out))
+    rc = lib().orc_gat_forward_train(_pf(_f(x)), n, fin, _pu(_u(edge_index)), num_edges,
+                                     _pf(_f(weight)), _pf(_f(att_src)), _pf(_f(att_dst)),
+                                     _pf(_f(bias)), heads, c, float(negative_slope), int(concat),
+                                     int(add_self_loops), float(dropout),
+                                     int(seed) & (2 ** 64 - 1), _pf(out))
     assert rc == 0
     return out
 
@@ -332,4 +349,86 @@ def sage_forward_csr(row_ptr, src_of, n, x, fin, aggr, lin_neighbor, lin_self, b
                                     SAGE_AGGR[aggr], _pf(_f(lin_neighbor)), _pf(_f(lin_self)),
                                     _pf(_f(bias)), fout, int(relu), threads, _pf(out))
     assert rc == 0
+    return out
+
+
+# ---- model zoo: src/nn/linear.ts, src/nn/activation.ts, src/core/tensor.ts ----
+def linear(x, w, b=None):
+    """Linear.forward (src/nn/linear.ts:50-111); x [m, k], w [n, k]."""
+    x = _f(x)
+    w = _f(w)
+    n, k = w.shape
+    m = x.size // k
+    out = np.empty((m, n), np.float32)
+    lib().orc_linear(_pf(x), m, k, _pf(w), _pf(_f(b)), n, _pf(out))
+    return out
+
+
+def _unary(name, x):
+    x = _f(x)
+    out = np.empty_like(x)
+    getattr(lib(), name)(_pf(x), x.size, _pf(out))
+    return out
+
+
+def sigmoid(x):
+    return _unary("orc_sigmoid", x)
+
+
+def tanh(x):
+    return _unary("orc_tanh", x)
+
+
+def gelu(x):
+    return _unary("orc_gelu", x)
+
+
+def silu(x):
+    return _unary("orc_silu", x)
+
+
+def prelu(x, w):
+    x, w = _f(x), _f(w)
+    out = np.empty_like(x)
+    lib().orc_prelu(_pf(x), x.size, _pf(w), w.size, _pf(out))
+    return out
+
+
+def softmax_rows(x, col_mask=None, mask_value=-1e9, log=False):
+    """Tensor.softmax / logSoftmax of a 2-D array (src/core/tensor.ts:435-499)."""
+    x = _f(x)
+    rows, cols = x.shape
+    out = np.empty_like(x)
+    m = None
+    if col_mask is not None:
+        m = np.ascontiguousarray(col_mask, dtype=np.uint8)
+    lib().orc_softmax_rows(_pf(x), rows, cols,
+                           None if m is None else m.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)),
+                           float(mask_value), int(bool(log)), _pf(out))
+    return out
+
+
+def uniform(seed, i):
+    return float(lib().orc_uniform(int(seed) & (2 ** 64 - 1), int(i)))
+
+
+def dropout(x, p, seed):
+    x = _f(x)
+    out = np.empty_like(x)
+    lib().orc_dropout(_pf(x), x.size, float(p), int(seed) & (2 ** 64 - 1), _pf(out))
+    return out
+
+
+LINK_MODES = {"dot": 0, "bilinear": 1, "mlp": 2}
+
+
+def link_scores(emb, src, tgt, mode, w_bilinear=None, w1=None, b1=None, w2=None, b2=None):
+    """ConceptPrerequisiteMapper.predictLinks (ConceptPrerequisiteMapper.ts:224-295)."""
+    emb = _f(emb)
+    d = emb.shape[1]
+    src, tgt = _u(src), _u(tgt)
+    out = np.empty(src.size, np.float64)
+    lib().orc_link_scores(_pf(emb), d, _pu(src), _pu(tgt), src.size, LINK_MODES[mode],
+                          _pf(_f(w_bilinear)), _pf(_f(w1)), _pf(_f(b1)), _pf(_f(w2)),
+                          _pf(_f(b2)), out.ctypes.data_as(ctypes.POINTER(ctypes.c_double)))
     return out
