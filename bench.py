@@ -156,7 +156,7 @@ def build_layers(weights, device):
 def sage_forward(layers, dg, x, exchange=None, timers=None):
     """Three SAGEConv layers (aggregate -> fused dual GEMM + bias + ReLU).
     `exchange(x_local) -> x_ext` fills halo rows for a partitioned graph.
-    `timers` collects CUDA events around each aggregation launch."""
+    `timers` collects CUDA events around each phase (exchange, aggregate, linear)."""
     import torch
 
     from browsergnn_b200.backend import ptr
@@ -164,25 +164,108 @@ def sage_forward(layers, dg, x, exchange=None, timers=None):
     ctx = dg.ctx
     n_own = dg.num_dst
     h = x
+
+    def mark():
+        if timers is None:
+            return None
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        return ev
+
     for li, lay in enumerate(layers):
         fin, fout = lay.inChannels, lay.outChannels
+        e0 = mark()
         src = exchange(h) if exchange is not None else h
         agg = torch.empty((n_own, fin), dtype=torch.float32, device=h.device)
-        if timers is not None:
-            ev0 = torch.cuda.Event(enable_timing=True)
-            ev1 = torch.cuda.Event(enable_timing=True)
-            ev0.record()
+        e1 = mark()
         ctx.call("bgnn_aggregate", dg.h, 1, ptr(src), fin, ptr(agg))
-        if timers is not None:
-            ev1.record()
-            timers.append((li, fin, ev0, ev1))
+        e2 = mark()
         out = torch.empty((n_own, fout), dtype=torch.float32, device=h.device)
         act = 1 if li < len(layers) - 1 else 0  # ReLU between layers (wasmRelu)
         ctx.call("bgnn_sage_linear", ptr(agg), ptr(h), ptr(lay.p("lin_neighbor")),
                  ptr(lay.p("lin_self")), n_own, fin, fout, ptr(lay.p("bias")), act, 0.0,
                  ptr(out))
+        e3 = mark()
+        if timers is not None:
+            timers.append((li, fin, e1, e2, e0, e3))
         h = out
     return h
+
+
+class PartitionedSage:
+    """The same three layers on one rank of a row partition.  Buffers are
+    allocated once: per layer an [owned | halo] feature buffer whose owned
+    rows the previous layer writes directly, so the exchange only fills the
+    halo rows.  For outputs wider than 64 the self product x*W_self runs on a
+    side stream while the halo rows are in flight; the neighbour product then
+    adds to it (bgnn_linear_add), the same two f32 results and the same final
+    rounding as bgnn_sage_linear."""
+
+    def __init__(self, layers, part, dg, x, ctx):
+        import torch
+
+        self.layers, self.part, self.dg, self.ctx = layers, part, dg, ctx
+        n_own, n_ext = part.n_own, part.n_own + part.n_halo
+        dev = x.device
+        self.ext = [torch.empty((n_ext, lay.inChannels), dtype=torch.float32, device=dev)
+                    for lay in layers]
+        self.ext[0][:n_own].copy_(x)
+        self.agg = [torch.empty((n_own, lay.inChannels), dtype=torch.float32, device=dev)
+                    for lay in layers]
+        self.st = [torch.empty((n_own, lay.outChannels), dtype=torch.float32, device=dev)
+                   for lay in layers]
+        self.out = torch.empty((n_own, layers[-1].outChannels), dtype=torch.float32, device=dev)
+        self.side = torch.cuda.Stream(device=dev)
+        from browsergnn_b200.partition import cuda_pack
+
+        self.pack = cuda_pack(ctx)
+
+    def forward(self, timers=None):
+        import torch
+
+        from browsergnn_b200.backend import ptr
+
+        ctx, part, dg = self.ctx, self.part, self.dg
+        n_own = part.n_own
+        main = torch.cuda.current_stream()
+
+        def mark():
+            if timers is None:
+                return None
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            return ev
+
+        nl = len(self.layers)
+        for li, lay in enumerate(self.layers):
+            fin, fout = lay.inChannels, lay.outChannels
+            ext, agg = self.ext[li], self.agg[li]
+            out = self.ext[li + 1][:n_own] if li + 1 < nl else self.out
+            act = 1 if li < nl - 1 else 0
+            split = fout > 64
+            if split:
+                # x * W_self needs only the owned rows: start it before the exchange
+                self.side.wait_stream(main)
+                with torch.cuda.stream(self.side):
+                    ctx.call("bgnn_linear", ptr(ext), ptr(lay.p("lin_self")), n_own, fin, fout,
+                             None, 0, 0.0, ptr(self.st[li]))
+            e0 = mark()
+            part.exchange_into(ext, self.pack)
+            e1 = mark()
+            ctx.call("bgnn_aggregate", dg.h, 1, ptr(ext), fin, ptr(agg))
+            e2 = mark()
+            if split:
+                main.wait_stream(self.side)
+                ctx.call("bgnn_linear_add", ptr(agg), ptr(lay.p("lin_neighbor")), n_own, fin,
+                         fout, ptr(self.st[li]), ptr(lay.p("bias")), act, 0.0, ptr(out))
+            else:
+                ctx.call("bgnn_sage_linear", ptr(agg), ptr(ext), ptr(lay.p("lin_neighbor")),
+                         ptr(lay.p("lin_self")), n_own, fin, fout, ptr(lay.p("bias")), act,
+                         0.0, ptr(out))
+            e3 = mark()
+            if timers is not None:
+                timers.append((li, fin, e1, e2, e0, e3))
+        return self.out
 
 
 # ---------------------------------------------------------------------------
@@ -541,20 +624,20 @@ def main():
 
     t0 = time.perf_counter()
     if world > 1:
-        from browsergnn_b200.partition import HaloPlan, cuda_pack
+        from browsergnn_b200.partition import HaloPlan
 
         part = HaloPlan(ei[:e], ei[e:], n, rank, world)
         dg = part.device_graph(local)
         x = x_full[part.lo:part.hi].contiguous()
-        pack = cuda_pack(ctx)
-        exchange = lambda h: part.exchange(h, pack)  # noqa: E731
+        psage = PartitionedSage(layers, part, dg, x, ctx)
+        step = psage.forward
     else:
         from browsergnn_b200.graph import DeviceGraph
 
         dg = DeviceGraph(ei, e, n, n, device=local)
         x = x_full
-        exchange = None
         part = None
+        step = lambda timers=None: sage_forward(layers, dg, x, None, timers)  # noqa: E731
     torch.cuda.synchronize()
     build_s = time.perf_counter() - t0
     del x_full
@@ -565,7 +648,7 @@ def main():
         torch.cuda.synchronize()
 
     for _ in range(args.warmup):
-        sage_forward(layers, dg, x, exchange)
+        step()
     barrier()
     sampler = ClockSampler(local)
     sampler.start()
@@ -576,7 +659,7 @@ def main():
     barrier()
     start.record()
     for _ in range(args.steps):
-        sage_forward(layers, dg, x, exchange, timers)
+        step(timers)
     stop.record()
     barrier()
     clocks = sampler.stop()
@@ -591,8 +674,22 @@ def main():
 
     # roofline of the dominant kernel: the F=256 aggregation (layers 2 and 3)
     agg_ms = {}
-    for li, fin, a, b in timers:
+    phases = {}  # per layer: exchange, aggregate, linear (ms, mean over steps)
+    for li, fin, a, b, x0, l1 in timers:
         agg_ms.setdefault((li, fin), []).append(a.elapsed_time(b))
+        ph = phases.setdefault(li, [[], [], []])
+        ph[0].append(x0.elapsed_time(a))
+        ph[1].append(a.elapsed_time(b))
+        ph[2].append(b.elapsed_time(l1))
+    phase_vec = [statistics.mean(v) for li in sorted(phases) for v in phases[li]]
+    if world > 1:
+        pv = torch.tensor(phase_vec, device="cuda", dtype=torch.float64)
+        dist.all_reduce(pv, op=dist.ReduceOp.MAX)
+        phase_vec = pv.tolist()
+    phase_ms = {f"L{li + 1}": {"exchange": round(phase_vec[3 * i], 3),
+                               "aggregate": round(phase_vec[3 * i + 1], 3),
+                               "linear": round(phase_vec[3 * i + 2], 3)}
+                for i, li in enumerate(sorted(phases))}
     n_dst = dg.num_dst
     e_loc = dg.num_edges
     f = 256
@@ -668,6 +765,7 @@ def main():
                        "graph_build_s": round(build_s, 3)},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
             "clocks": clocks, "gpu_launches": launches,
+            "phase_ms_max_over_ranks": phase_ms,
         }
         if part is not None:
             line["config"]["halo_rows_rank0"] = part.n_halo

@@ -92,6 +92,7 @@ SIGNATURES = {
     "bgnn_graph_spmm": [_P, _P, _P, _P, _U32, _P],
     "bgnn_linear": [_P, _P, _P, _U32, _U32, _U32, _P, _I, _D, _P],
     "bgnn_sage_linear": [_P, _P, _P, _P, _P, _U32, _U32, _U32, _P, _I, _D, _P],
+    "bgnn_linear_add": [_P, _P, _P, _U32, _U32, _U32, _P, _P, _I, _D, _P],
     "bgnn_l2_normalize_rows": [_P, _P, _U32, _U32],
     "bgnn_sum_pool": [_P, _P, _U32, _U32, _P, _U32, _P],
     "bgnn_pack_rows": [_P, _P, _U32, _P, _U32, _U32, _P],

@@ -19,8 +19,8 @@
 //   streaming (k_agg_stream, the default): a persistent kernel pulls work
 //               items (each heavy row alone, largest first, then runs of light
 //               rows) from a queue; a pipe of threads streams an item's source
-//               rows into a 3-stage shared-memory ring with one bulk copy per
-//               edge and reduces them in edge order (see below).
+//               rows into a 3-stage shared-memory ring with 16-byte cp.async
+//               copies and reduces them in edge order (see below).
 //   light/heavy pair (k_agg_light + k_agg_heavy): only for the appended
 //               self-loop edge of GCN/GAT loop insertion.  Light rows: a group
 //               of G lanes per row, lanes over features; heavy rows: one CTA per
@@ -187,51 +187,6 @@ __device__ __forceinline__ void cp_async4(void* s, const void* g) {
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 
-// ---- mbarrier + bulk copy (TMA engine, non-tensor form) ----------------------
-__device__ __forceinline__ void mbar_init(uint64_t* bar, int count) {
-  const unsigned a = (unsigned)__cvta_generic_to_shared(bar);
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(a), "r"(count) : "memory");
-}
-__device__ __forceinline__ void fence_mbar_init() {
-  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-}
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-}
-__device__ __forceinline__ void mbar_arrive_expect_tx(unsigned bar, unsigned bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes)
-               : "memory");
-}
-// global -> shared bulk copy completing `bytes` on the mbarrier (no multicast)
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, unsigned bar) {
-  const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(d),
-      "l"(src), "r"(bytes), "r"(bar)
-      : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(unsigned bar, unsigned parity) {
-  unsigned ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Waits for the phase with the given parity to complete; gives up after about
-// 2^32 SM cycles (~2 s) so a lost copy can never hang the GPU.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
-  const unsigned a = (unsigned)__cvta_generic_to_shared(bar);
-  if (mbar_try_wait(a, parity)) return true;
-  const long long t0 = clock64();
-  for (;;) {
-    if (mbar_try_wait(a, parity)) return true;
-    if (clock64() - t0 > (1ll << 32)) return false;
-  }
-}
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
@@ -352,34 +307,20 @@ __device__ __forceinline__ void pipe_bar(int id, int count) {
     asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
 }
 
-// barrier that also returns the OR of `pred` over the pipe's threads, so every
-// thread takes the same decision
-__device__ __forceinline__ bool pipe_bar_or(int id, int count, bool pred) {
-  if (id == 0) return __syncthreads_or(pred ? 1 : 0) != 0;
-  unsigned r;
-  asm volatile(
-      "{\n\t.reg .pred q, p;\n\t"
-      "setp.ne.u32 q, %1, 0;\n\t"
-      "barrier.red.or.pred p, %2, %3, q;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(r)
-      : "r"(pred ? 1u : 0u), "r"(id), "r"(count)
-      : "memory");
-  return r != 0;
-}
-
-// how a stage's source rows reach shared memory
+// how a stage's source rows reach shared memory.  (One bulk copy per edge
+// through the TMA engine, completing on an mbarrier, measured slower at every
+// width: 14.0 vs 13.4 ms at F = 256, 8.0 vs 7.1 ms at F = 100, 18.6 vs
+// 17.3 ms for the F = 32 SpMM.)
 enum : int {
-  CP_BULK = 0,  // one bulk copy (TMA engine) per edge, completing on the slot's mbarrier
-  CP_A16 = 1,   // 16-byte cp.async copies spread over the pipe (narrow rows: many per warp)
-  CP_A4 = 2,    // 4-byte cp.async copies (rows not 16-byte aligned)
+  CP_A16 = 0,  // 16-byte cp.async copies spread over the pipe
+  CP_A4 = 1,   // 4-byte cp.async copies (rows not 16-byte aligned)
 };
 
 template <int OP, int CP>
-__device__ __forceinline__ bool stream_range(const AggArgs& a, uint32_t rb, uint32_t re, int f0,
+__device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint32_t re, int f0,
                                              int fw, int swp, int tp, int ptid, int eps,
                                              float* buf, float* wbuf, uint32_t* sidx, uint32_t* rps,
-                                             float* rdv, uint64_t* mbar, uint32_t& kg,
+                                             float* rdv, uint32_t& kg,
                                              int bar_id) {
   const uint32_t e0 = a.row_ptr[rb];
   const uint32_t ne = a.row_ptr[re] - e0;
@@ -400,26 +341,16 @@ __device__ __forceinline__ bool stream_range(const AggArgs& a, uint32_t rb, uint
     if (ptid < eps && m < nst && e < ne)
       cp_async4(sidx + (m % (ST_S + 1)) * eps + ptid, a.src_of + e0 + e);
   };
-  // CP_BULK: thread j < eps copies edge j's whole row slice with one bulk
-  // copy that completes on the slot's mbarrier; lane 0 of every warp of the
-  // pipe arrives for its warp with the bytes the warp's copies bring
-  // (arrival count = warps per pipe).  CP_A16 / CP_A4: cp.async copies of 16
-  // or 4 bytes spread over the pipe.  Per-edge weights always use cp.async.
+  // Row slices move as cp.async copies of 16 (CP_A16) or 4 bytes spread over
+  // the pipe, consecutive threads on consecutive chunks of one row; per-edge
+  // weights (GCN dinv, SpMM values) as 4-byte cp.async by the edge's thread.
   auto issue = [&](uint32_t k) {
     if (k < nst) {
       const int slot = (int)((kg + k) % ST_S);
       const uint32_t* sid = sidx + (k % (ST_S + 1)) * eps;
       const int cnt = (int)min((uint32_t)eps, ne - k * (uint32_t)eps);  // edges in this stage
       float* sb = buf + (size_t)slot * eps * swp;
-      if (CP == CP_BULK) {
-        const bool mine = ptid < cnt;
-        const unsigned have = __ballot_sync(0xffffffffu, mine);
-        const uint32_t mb = (uint32_t)__cvta_generic_to_shared(mbar + slot);
-        if ((ptid & 31) == 0) mbar_arrive_expect_tx(mb, (unsigned)__popc(have) * row_bytes);
-        __syncwarp();
-        if (mine)
-          bulk_g2s(sb + (size_t)ptid * swp, a.x + (int64_t)sid[ptid] * a.ld_x + f0, row_bytes, mb);
-      } else if (CP == CP_A16) {
+      if (CP == CP_A16) {
         const int ch = fw >> 2;  // 16-byte chunks per edge (fw is a multiple of 4 here)
         const int copies = cnt * ch;
         for (int c = ptid; c < copies; c += tp) {
@@ -452,8 +383,6 @@ __device__ __forceinline__ bool stream_range(const AggArgs& a, uint32_t rb, uint
       if (m < nst && e < ne) sidx[m * eps + ptid] = a.src_of[e0 + e];
     }
   }
-  constexpr bool BULK = CP == CP_BULK;
-  if (BULK) fence_proxy_async_smem();
   pipe_bar(bar_id, tp);
 #pragma unroll
   for (int k = 0; k < ST_S - 1; k++) issue((uint32_t)k);
@@ -473,25 +402,10 @@ __device__ __forceinline__ bool stream_range(const AggArgs& a, uint32_t rb, uint
       if (OP == OP_GCN) dinv_r = rdv[r];
     }
   };
-  bool ok = true;
   for (uint32_t k = 0; k < nst; k++) {
     const int slot = (int)((kg + k) % ST_S);
-    cp_async_wait<ST_S - 2>();
-    bool timed_out = false;
-    if (BULK && !mbar_wait(mbar + slot, ((kg + k) / ST_S) & 1u)) {
-      dev_raise(a.err, DEVERR_TIMEOUT, (uint64_t)rb, 3);
-      timed_out = true;
-    }
-    if (BULK) {
-      // a bounded wait ran out somewhere in the pipe: every thread leaves together
-      if (pipe_bar_or(bar_id, tp, timed_out)) {
-        ok = false;
-        break;
-      }
-    } else {
-      pipe_bar(bar_id, tp);
-    }
-    if (BULK) fence_proxy_async_smem();  // generic reads of the freed slot before async writes
+    cp_async_wait<ST_S - 2>();  // this thread's copies of stage k have landed
+    pipe_bar(bar_id, tp);       // ... and everyone's; stage k-1's slot is free
     issue(k + ST_S - 1);
     if (consumer) {
       const float* b = buf + (size_t)slot * eps * swp + ptid;
@@ -533,26 +447,22 @@ __device__ __forceinline__ bool stream_range(const AggArgs& a, uint32_t rb, uint
     }
   }
   cp_async_wait<0>();
-  if (ok) {
-    kg += nst;
-    if (consumer)
-      while (r < nrows) finalize();
-  }
+  kg += nst;
+  if (consumer)
+    while (r < nrows) finalize();
   pipe_bar(bar_id, tp);  // the ring and row buffer are reused by the next item
-  return ok;
 }
 
-template <int OP, bool BULK>
+template <int OP, bool A16>
 __global__ void __launch_bounds__(ST_THREADS, 2)
     k_agg_stream(const AggArgs a, int P, int swp, int n_slices, uint32_t n_giant, int gsw,
                  int eps_g, uint32_t* queue) {
   extern __shared__ float4 st_smem4[];
   float* data = reinterpret_cast<float*>(st_smem4);
   const size_t data_f = stream_data_floats(P, swp);
-  // after the ring: mbarriers (heavy set, one set per pipe), then per-edge
-  // weights, source ids, row offsets, fetched items, GCN row dinv
-  uint64_t* mbar = reinterpret_cast<uint64_t*>(data + data_f);
-  float* wb = reinterpret_cast<float*>(mbar + (P + 1) * ST_S);
+  // after the ring: per-edge weights, source ids, row offsets, fetched
+  // items, GCN row dinv
+  float* wb = data + data_f;
   uint32_t* sidx = reinterpret_cast<uint32_t*>(wb + stream_w_floats(P));
   uint32_t* rps = sidx + stream_sidx_words(P);
   int* slots = reinterpret_cast<int*>(rps + P * (ST_RMAX + 1));  // [0..P] fetched items
@@ -563,47 +473,30 @@ __global__ void __launch_bounds__(ST_THREADS, 2)
   const uint32_t heavy_work = giant_work + (a.n_heavy_items - n_giant) * (uint32_t)n_slices;
   const uint32_t light_work = (a.n_items - a.n_heavy_items) * (uint32_t)n_slices;
   const int tp = ST_THREADS / P;
-  // heavy and light rows move by bulk copies when rows are 16-byte aligned;
-  // giant-row slices are narrow (many short rows per stage) and move by
-  // 16-byte cp.async, which spreads them over the whole CTA
-  constexpr int CP_MAIN = BULK ? CP_A16 : CP_A4;
-  constexpr int CP_GIANT = BULK ? CP_A16 : CP_A4;
-  uint64_t* mbar_heavy = mbar;
-  if (CP_MAIN == CP_BULK && threadIdx.x == 0) {
-    // one arrival per warp of the pipe and stage
-    for (int i = 0; i < ST_S; i++) mbar_init(mbar_heavy + i, ST_THREADS / 32);
-    for (int p = 0; p < P; p++)
-      for (int i = 0; i < ST_S; i++) mbar_init(mbar + (p + 1) * ST_S + i, ST_THREADS / P / 32);
-    fence_mbar_init();
-  }
-  __syncthreads();
+  constexpr int CP = A16 ? CP_A16 : CP_A4;  // rows 16-byte aligned: 16-byte copies
 
   // phase 1: heavy rows with the whole CTA as one pipe.  Giant rows (the
   // first n_giant heavy items, chosen at launch) are cut into gsw-feature
   // slices with eps_g edges per stage, so several CTAs stream one hub row at
   // once; each slice is still reduced in edge order by one thread per feature.
-  uint32_t kg_heavy = 0, kg_giant = 0;  // stages run so far (ring slot and mbarrier phase)
+  uint32_t kg = 0;  // stages run so far (ring slot)
   for (;;) {
     if (threadIdx.x == 0) slots[P] = (int)atomicAdd(&queue[0], 1u);
     __syncthreads();
     const uint32_t w = (uint32_t)slots[P];
     if (w >= heavy_work) break;
-    bool ok;
     if (w < giant_work) {
       const uint2 item = a.items[w / gs];
       const int f0 = (int)(w % gs) * gsw;
-      ok = stream_range<OP, CP_GIANT>(a, item.x, item.y, f0, min(gsw, F - f0), gsw, ST_THREADS,
-                                      threadIdx.x, eps_g, data, wb, sidx, rps, rdv, nullptr,
-                                      kg_giant, 0);
+      stream_range<OP, CP>(a, item.x, item.y, f0, min(gsw, F - f0), gsw, ST_THREADS,
+                                threadIdx.x, eps_g, data, wb, sidx, rps, rdv, kg, 0);
     } else {
       const uint32_t w2 = w - giant_work;
       const uint2 item = a.items[n_giant + w2 / (uint32_t)n_slices];
       const int f0 = (int)(w2 % (uint32_t)n_slices) * ST_SW;
-      ok = stream_range<OP, CP_MAIN>(a, item.x, item.y, f0, min(ST_SW, F - f0), swp, ST_THREADS,
-                                     threadIdx.x, ST_EPS * P, data, wb, sidx, rps, rdv,
-                                     mbar_heavy, kg_heavy, 0);
+      stream_range<OP, CP>(a, item.x, item.y, f0, min(ST_SW, F - f0), swp, ST_THREADS,
+                           threadIdx.x, ST_EPS * P, data, wb, sidx, rps, rdv, kg, 0);
     }
-    if (!ok) return;
   }
   // phase 2: light items, P independent pipes
   const int pipe = threadIdx.x / tp, ptid = threadIdx.x % tp;
@@ -613,7 +506,6 @@ __global__ void __launch_bounds__(ST_THREADS, 2)
   uint32_t* psidx = sidx + pipe * (ST_S + 1) * ST_EPS;
   uint32_t* prps = rps + pipe * (ST_RMAX + 1);
   float* prdv = rdv + pipe * ST_RMAX;
-  uint64_t* pmbar = mbar + (pipe + 1) * ST_S;
   uint32_t kgp = 0;
   for (;;) {
     if (ptid == 0) slots[pipe] = (int)atomicAdd(&queue[1], 1u);
@@ -622,21 +514,20 @@ __global__ void __launch_bounds__(ST_THREADS, 2)
     if (w >= light_work) break;
     const uint2 item = a.items[a.n_heavy_items + w / (uint32_t)n_slices];
     const int f0 = (int)(w % (uint32_t)n_slices) * ST_SW;
-    if (!stream_range<OP, CP_MAIN>(a, item.x, item.y, f0, min(ST_SW, F - f0), swp, tp, ptid,
-                                   ST_EPS, pdata, pwb, psidx, prps, prdv, pmbar, kgp, bar_id))
-      return;
+    stream_range<OP, CP>(a, item.x, item.y, f0, min(ST_SW, F - f0), swp, tp, ptid, ST_EPS, pdata,
+                         pwb, psidx, prps, prdv, kgp, bar_id);
   }
 }
 
-template <int OP, bool BULK>
+template <int OP, bool A16>
 int launch_stream_t(bgnn_ctx* ctx, const AggArgs& a, int P, int swp, int n_slices) {
-  size_t smem = stream_data_floats(P, swp) * 4 + (size_t)(P + 1) * ST_S * 8 +
-                (stream_w_floats(P) + stream_sidx_words(P) + (size_t)P * (ST_RMAX + 1) + 16) * 4;
+  size_t smem = (stream_data_floats(P, swp) + stream_w_floats(P) + stream_sidx_words(P) +
+                 (size_t)P * (ST_RMAX + 1) + 16) * 4;
   if (OP == OP_GCN) smem += (size_t)P * ST_RMAX * 4;
-  BGNN_CUDA(ctx, cudaFuncSetAttribute(k_agg_stream<OP, BULK>,
+  BGNN_CUDA(ctx, cudaFuncSetAttribute(k_agg_stream<OP, A16>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   int per_sm = 0;
-  BGNN_CUDA(ctx, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_agg_stream<OP, BULK>,
+  BGNN_CUDA(ctx, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_agg_stream<OP, A16>,
                                                                ST_THREADS, smem));
   if (per_sm < 1) per_sm = 1;
   const uint64_t work = (uint64_t)a.n_items * n_slices;
@@ -662,7 +553,7 @@ int launch_stream_t(bgnn_ctx* ctx, const AggArgs& a, int P, int swp, int n_slice
   const int eps_g = ST_GSTAGE / gsw;  // edges per giant stage (at most ST_THREADS)
   uint32_t* queue = ctx->d_small;
   BGNN_CUDA(ctx, cudaMemsetAsync(queue, 0, 2 * sizeof(uint32_t), ctx->stream));
-  k_agg_stream<OP, BULK><<<(unsigned)grid, ST_THREADS, smem, ctx->stream>>>(
+  k_agg_stream<OP, A16><<<(unsigned)grid, ST_THREADS, smem, ctx->stream>>>(
       a, P, swp, n_slices, n_giant, gsw, eps_g, queue);
   BGNN_LAUNCHED(ctx);
   return BGNN_OK;
@@ -679,9 +570,9 @@ int launch_stream(bgnn_ctx* ctx, const AggArgs& a0) {
   while (pw < swp) pw <<= 1;
   const int P = ST_THREADS / pw;  // 1, 2, 4 or 8
   const int n_slices = (F + ST_SW - 1) / ST_SW;
-  // bulk copies need 16-byte aligned rows and sizes: F % 4 == 0 covers every slice
-  const bool bulk = (F % 4 == 0) && ((uintptr_t)a.x % 16 == 0) && (a.ld_x % 4 == 0);
-  return bulk ? launch_stream_t<OP, true>(ctx, a, P, swp, n_slices)
+  // 16-byte copies need 16-byte aligned rows: F % 4 == 0 covers every slice
+  const bool a16 = (F % 4 == 0) && ((uintptr_t)a.x % 16 == 0) && (a.ld_x % 4 == 0);
+  return a16 ? launch_stream_t<OP, true>(ctx, a, P, swp, n_slices)
               : launch_stream_t<OP, false>(ctx, a, P, swp, n_slices);
 }
 

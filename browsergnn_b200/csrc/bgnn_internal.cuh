@@ -196,6 +196,10 @@ int bgnn_run_gat(bgnn_ctx* ctx, const bgnn_graph* g, const float* h, uint32_t he
 int bgnn_run_linear(bgnn_ctx* ctx, const float* a, const float* w, const float* a2,
                     const float* w2, uint32_t m, uint32_t k, uint32_t n, const float* bias,
                     int act, double act_param, float* out);
+// out = act(f32(f32(addend + a*w) + bias)), the a*w chain k-ascending per output
+int bgnn_run_linear_add(bgnn_ctx* ctx, const float* a, const float* w, uint32_t m, uint32_t k,
+                        uint32_t n, const float* addend, const float* bias, int act,
+                        double act_param, float* out);
 int bgnn_run_activation(bgnn_ctx* ctx, int act, double param, const float* x, uint64_t n,
                         float* out);
 int bgnn_run_add(bgnn_ctx* ctx, const float* a, const float* b, uint64_t n, float* out);

@@ -482,6 +482,16 @@ extern "C" int bgnn_sage_linear(bgnn_ctx* ctx, const float* agg, const float* x,
                          act_param, out);
 }
 
+extern "C" int bgnn_linear_add(bgnn_ctx* ctx, const float* a, const float* w, uint32_t m,
+                               uint32_t k, uint32_t n, const float* addend, const float* bias,
+                               int act, double act_param, float* out) {
+  BGNN_TRY(ctx_ok(ctx));
+  BGNN_TRY(check_act(ctx, act));
+  BGNN_REQUIRE(ctx, (a && w) || (uint64_t)m * k * n == 0, "NULL operand");
+  BGNN_REQUIRE(ctx, (addend && out) || (uint64_t)m * n == 0, "NULL addend/out");
+  return bgnn_run_linear_add(ctx, a, w, m, k, n, addend, bias, act, act_param, out);
+}
+
 extern "C" int bgnn_l2_normalize_rows(bgnn_ctx* ctx, float* x, uint32_t m, uint32_t n) {
   BGNN_TRY(ctx_ok(ctx));
   BGNN_REQUIRE(ctx, x || (uint64_t)m * n == 0, "NULL x");

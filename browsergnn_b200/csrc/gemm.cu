@@ -396,6 +396,14 @@ int bgnn_run_linear(bgnn_ctx* ctx, const float* a, const float* w, const float* 
   return dual ? pick_tile<false, true>(ctx, g) : pick_tile<false, false>(ctx, g);
 }
 
+int bgnn_run_linear_add(bgnn_ctx* ctx, const float* a, const float* w, uint32_t m, uint32_t k,
+                        uint32_t n, const float* addend, const float* bias, int act,
+                        double act_param, float* out) {
+  if (m == 0 || n == 0) return BGNN_OK;
+  return launch_sgemm128(ctx, a, w, m, k, n, addend, bias, act, act_param, out,
+                         ctx->math == BGNN_MATH_EXACT);
+}
+
 int bgnn_run_activation(bgnn_ctx* ctx, int act, double param, const float* x, uint64_t n,
                         float* out) {
   if (n == 0) return BGNN_OK;

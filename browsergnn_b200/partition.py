@@ -101,6 +101,22 @@ class HaloPlan:
                                group=self.group)
         return ext
 
+    def exchange_into(self, ext, pack: Callable):
+        """Fill the halo rows ext[n_own:] of a buffer whose owned rows
+        ext[:n_own] already hold this rank's features (no copy of the owned
+        part)."""
+        import torch.distributed as dist
+
+        torch = _torch()
+        f = int(ext.shape[1])
+        own = ext[: self.n_own]
+        send = torch.empty((self.n_send, f), dtype=ext.dtype, device=ext.device)
+        if self.n_send:
+            pack(own, self.send_rows, send)
+        dist.all_to_all_single(ext[self.n_own:], send, self.recv_splits, self.send_splits,
+                               group=self.group)
+        return ext
+
     def device_graph(self, device: Optional[int] = None):
         from .graph import DeviceGraph
 

@@ -256,6 +256,15 @@ BGNN_API int bgnn_linear(bgnn_ctx* ctx, const float* a, const float* w, uint32_t
 BGNN_API int bgnn_sage_linear(bgnn_ctx* ctx, const float* agg, const float* x, const float* w_neigh,
                      const float* w_self, uint32_t m, uint32_t k, uint32_t n,
                      const float* bias, int act, double act_param, float* out);
+/* The second half of bgnn_sage_linear as its own call: out = act(f32(f32(
+ * addend + a*w) + bias)), a*w accumulated k-ascending per output exactly as
+ * bgnn_linear.  With addend = x*w_self from bgnn_linear this is
+ * bgnn_sage_linear split in two (SAGEConv.forward, sage.ts:171-196), so the
+ * self product can run while the neighbour rows are still being exchanged.
+ * addend may alias out. */
+BGNN_API int bgnn_linear_add(bgnn_ctx* ctx, const float* a, const float* w, uint32_t m,
+                             uint32_t k, uint32_t n, const float* addend, const float* bias,
+                             int act, double act_param, float* out);
 /* SAGE 'pool' aggregator projection (sage.ts:149-159) applied per node:
  * out[i,j] = f32(Math.max(0, bias[j] + sum_q x[i,q]*w[q,j])) with a double
  * accumulator; w is [k, k].  An edge's projected message depends only on its

@@ -315,3 +315,40 @@ def test_training_mode_forward_runs(bg):
     assert_bits_equal(t1, t2, "same seed, same draws")
     ev = m.eval().forward(g).cpu().numpy()
     assert not np.allclose(ev, t1)
+
+
+@pytest.mark.parametrize("n", [47, 256])
+def test_linear_add_is_sage_linear_split(bg, n):
+    """bgnn_linear (self product) then bgnn_linear_add (neighbour product
+    added to it) gives bgnn_sage_linear's bits."""
+    import torch
+
+    rng = np.random.default_rng(n)
+    m, k = 700, 96
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    agg = rng.standard_normal((m, k)).astype(np.float32)
+    ws = (rng.standard_normal((k, n)) * 0.1).astype(np.float32)
+    wn = (rng.standard_normal((k, n)) * 0.1).astype(np.float32)
+    b = rng.standard_normal(n).astype(np.float32)
+    d = {kk: _dev(v) for kk, v in dict(x=x, agg=agg, ws=ws, wn=wn, b=b).items()}
+    ctx = bg.get_context()
+    ctx.set_math(True)
+    try:
+        st = torch.empty((m, n), dtype=torch.float32, device="cuda")
+        out = torch.empty_like(st)
+        ref = torch.empty_like(st)
+        ctx.call("bgnn_linear", d["x"].data_ptr(), d["ws"].data_ptr(), m, k, n, None, 0, 0.0,
+                 st.data_ptr())
+        ctx.call("bgnn_linear_add", d["agg"].data_ptr(), d["wn"].data_ptr(), m, k, n,
+                 st.data_ptr(), d["b"].data_ptr(), 1, 0.0, out.data_ptr())
+        ctx.call("bgnn_sage_linear", d["agg"].data_ptr(), d["x"].data_ptr(), d["wn"].data_ptr(),
+                 d["ws"].data_ptr(), m, k, n, d["b"].data_ptr(), 1, 0.0, ref.data_ptr())
+    finally:
+        ctx.set_math(False)
+    assert_bits_equal(out.cpu().numpy(), ref.cpu().numpy(), "split vs fused")
+    # the oracle's SAGE combine (sage.ts:171-196): f32(St + Nt), + bias, ReLU
+    st_o = orc.matmul(x, ws, m, k, n).reshape(m, n)
+    nt_o = orc.matmul(agg, wn, m, k, n).reshape(m, n)
+    comb = (st_o.astype(np.float64) + nt_o).astype(np.float32)
+    comb = (comb.astype(np.float64) + b).astype(np.float32)
+    assert_bits_equal(out.cpu().numpy(), orc.relu(comb), "vs oracle")

@@ -41,6 +41,11 @@ def _rank_main(rank, world, port, n, f, ei, e, x, want, q):
         ext = plan.exchange(xl, pack).numpy()
         need = np.concatenate([np.arange(plan.lo, plan.hi), plan.halo.numpy()]).astype(np.int64)
         ok_ext = np.array_equal(ext, x[need])
+        # in-place variant: owned rows already in the buffer, only halo rows move
+        buf = torch.full((plan.n_own + plan.n_halo, f), float("nan"))
+        buf[: plan.n_own].copy_(xl)
+        plan.exchange_into(buf, pack)
+        ok_ext = ok_ext and np.array_equal(buf.numpy(), x[need])
         lei = plan.edge_index.numpy().view(np.uint32)
         rp, so, _ = orc.dst_csr(np.concatenate([lei[:plan.num_edges], lei[plan.num_edges:]]),
                                 plan.num_edges, plan.n_own)
