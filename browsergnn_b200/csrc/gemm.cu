@@ -283,6 +283,282 @@ int launch_sgemm128(bgnn_ctx* ctx, const float* a, const float* b, uint32_t m, u
   return BGNN_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Multistage X*W: the same per-output k-ascending chain as k_sgemm128, with
+// both operands moved by cp.async into a 4-stage shared-memory ring so no
+// register staging or shared stores sit in the FMA stream.
+//   A [m, k] row-major goes in transposed (As[k][m]) with 4-byte copies:
+//     consecutive threads read consecutive k of one row (coalesced), and
+//     the thread's 8 rows for one k come back as two 16-byte shared loads.
+//   B [k, n] goes in as is, 16-byte copies when n % 4 == 0 (4-byte else).
+//   Rows, columns and k beyond the matrix are zero-filled by the copy
+//   (src-size 0) and never reach an output; the last partial k tile runs
+//   only its real k steps (no fma with padding: it could turn -0 into +0).
+// Tile 128 x BN (BN = 128: 8x8 per thread; BN = 64: 8x4), BK = 16.
+// ---------------------------------------------------------------------------
+constexpr int PG_BM = 128, PG_BK = 16, PG_S = 4, PG_APAD = 4;
+constexpr int PG_UNROLL = 16;  // k steps per unrolled block: keeps the loop in the instruction cache
+
+__device__ __forceinline__ void cpa4_zfill(float* s, const float* g, bool valid) {
+  const unsigned sa = (unsigned)__cvta_generic_to_shared(s);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(sa), "l"(g),
+               "r"(valid ? 4 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cpa16_zfill(float* s, const float* g, bool valid) {
+  const unsigned sa = (unsigned)__cvta_generic_to_shared(s);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(sa), "l"(g),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cpa_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cpa_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+template <int BN>
+constexpr size_t pg_smem_bytes() {
+  return (size_t)PG_S * (PG_BK * (PG_BM + PG_APAD) + PG_BK * BN) * sizeof(float);
+}
+
+template <int BN, bool EXACT, bool B16, bool V4OUT>
+__global__ void __launch_bounds__(256, 2) k_sgemm_pipe(const float* __restrict__ A,
+                                                       const float* __restrict__ B, uint32_t m,
+                                                       uint32_t k, uint32_t n,
+                                                       const float* addend,
+                                                       const float* __restrict__ bias, int act,
+                                                       double act_param, float* C) {
+  constexpr int TN = BN / 16;                 // 8 or 4 columns per thread
+  constexpr int AST = PG_BM + PG_APAD;        // As row stride (floats)
+  constexpr int A_STAGE = PG_BK * AST, B_STAGE = PG_BK * BN;
+  extern __shared__ float4 pg_smem4[];
+  float* smem = reinterpret_cast<float*>(pg_smem4);
+  float* As = smem;                           // [S][BK][AST]
+  float* Bs = smem + PG_S * A_STAGE;          // [S][BK][BN]
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  const uint64_t m0 = (uint64_t)blockIdx.x * PG_BM;
+  const uint32_t n0 = blockIdx.y * BN;
+  const uint32_t ntiles = (k + PG_BK - 1) / PG_BK;
+
+  // Per-thread copy pattern, fixed for every tile.  A: the thread copies
+  // columns a_kk and a_kk + 8 of rows a_r + 32 j (j < 4); a warp covers 4
+  // rows x 8 columns, 32-byte runs in global memory and 32 distinct banks in
+  // the transposed tile (row stride = 4 mod 32).  B (16-byte): rows b_kk +
+  // (256 / (BN/4)) i, columns b_c..b_c+3; B (4-byte): rows b_kk + (256 / BN) i,
+  // column b_c.
+  const int a_kk = tid % 8, a_r = tid / 8;
+  const float* a_src = A + (m0 + a_r) * k + a_kk;
+  float* a_dst = As + a_kk * AST + a_r;
+  constexpr int B_COLS = B16 ? BN / 4 : BN;       // copies per B row
+  constexpr int B_ROWS = 256 / B_COLS;            // B rows covered per pass
+  constexpr int B_PASSES = PG_BK / B_ROWS;
+  const int b_kk = tid / B_COLS, b_c = (tid % B_COLS) * (B16 ? 4 : 1);
+  const bool b_col_ok = n0 + b_c < n;
+  const float* b_src = B + (uint64_t)b_kk * n + n0 + b_c;
+  float* b_dst = Bs + b_kk * BN + b_c;
+
+  auto load_stage = [&](uint32_t t, int slot) {
+    const uint32_t k0 = t * PG_BK;
+#pragma unroll
+    for (int i = 0; i < (PG_BM * PG_BK) / 256; i++) {
+      const int dk = 8 * (i & 1), dr = 32 * (i >> 1);
+      const bool ok = k0 + a_kk + dk < k && m0 + a_r + dr < m;
+      cpa4_zfill(a_dst + slot * A_STAGE + dk * AST + dr,
+                 ok ? a_src + (uint64_t)dr * k + k0 + dk : A, ok);
+    }
+#pragma unroll
+    for (int i = 0; i < B_PASSES; i++) {
+      const uint32_t gk = k0 + b_kk + B_ROWS * i;
+      const bool ok = b_col_ok && gk < k;
+      const float* src = ok ? b_src + (uint64_t)(k0 + B_ROWS * i) * n : B;
+      float* dst = b_dst + slot * B_STAGE + B_ROWS * i * BN;
+      if constexpr (B16)
+        cpa16_zfill(dst, src, ok);
+      else
+        cpa4_zfill(dst, src, ok);
+    }
+  };
+
+  // FAST: two adjacent columns share one packed fma.rn.f32x2 (two IEEE f32
+  // fmas per instruction, each rounded exactly like fmaf), which halves the
+  // FMA instructions the schedulers issue.  EXACT: the double-emulated step.
+  constexpr int TP = TN / 2;
+  float acc[8][TN];
+  uint64_t accp[8][TP];  // FAST: (acc[i][2p], acc[i][2p+1]) packed
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+#pragma unroll
+    for (int j = 0; j < TN; j++) acc[i][j] = 0.0f;
+#pragma unroll
+    for (int q = 0; q < TP; q++) accp[i][q] = 0ull;
+  }
+
+  auto kstep = [&](const float* as, const float* bs, int kk) {
+    const float4 a0 = *reinterpret_cast<const float4*>(as + kk * AST + ty * 4);
+    const float4 a1 = *reinterpret_cast<const float4*>(as + kk * AST + 64 + ty * 4);
+    const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    if constexpr (!EXACT) {
+      uint64_t bp[TP];
+      const ulonglong2 q0 = *reinterpret_cast<const ulonglong2*>(bs + kk * BN + tx * 4);
+      bp[0] = q0.x;
+      bp[1] = q0.y;
+      if constexpr (TN == 8) {
+        const ulonglong2 q1 = *reinterpret_cast<const ulonglong2*>(bs + kk * BN + 64 + tx * 4);
+        bp[2] = q1.x;
+        bp[3] = q1.y;
+      }
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        uint64_t ad;
+        asm("mov.b64 %0, {%1, %1};" : "=l"(ad) : "f"(av[i]));
+#pragma unroll
+        for (int q = 0; q < TP; q++)
+          asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(accp[i][q]) : "l"(ad), "l"(bp[q]), "l"(accp[i][q]));
+      }
+      return;
+    }
+    float bv[TN];
+    const float4 b0 = *reinterpret_cast<const float4*>(bs + kk * BN + tx * 4);
+    bv[0] = b0.x; bv[1] = b0.y; bv[2] = b0.z; bv[3] = b0.w;
+    if constexpr (TN == 8) {
+      const float4 b1 = *reinterpret_cast<const float4*>(bs + kk * BN + 64 + tx * 4);
+      bv[4] = b1.x; bv[5] = b1.y; bv[6] = b1.z; bv[7] = b1.w;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+#pragma unroll
+      for (int j = 0; j < TN; j++) acc[i][j] = mac<EXACT>(av[i], bv[j], acc[i][j]);
+  };
+
+#pragma unroll
+  for (int t = 0; t < PG_S - 1; t++) {
+    if ((uint32_t)t < ntiles) load_stage(t, t);
+    cpa_commit();
+  }
+  for (uint32_t t = 0; t < ntiles; t++) {
+    cpa_wait<PG_S - 2>();  // this thread's copies of tile t have landed
+    __syncthreads();       // ... everyone's; and tile t-1's slot is free
+    if (t + PG_S - 1 < ntiles) load_stage(t + PG_S - 1, (int)((t + PG_S - 1) % PG_S));
+    cpa_commit();
+    const int slot = (int)(t % PG_S);
+    const float* as = As + slot * A_STAGE;
+    const float* bs = Bs + slot * B_STAGE;
+    const int kn = (int)min((uint32_t)PG_BK, k - t * PG_BK);  // the last tile may be partial
+#pragma unroll PG_UNROLL
+    for (int kk = 0; kk < kn; kk++) kstep(as, bs, kk);
+  }
+  cpa_wait<0>();
+  if constexpr (!EXACT) {
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+#pragma unroll
+      for (int q = 0; q < TP; q++)
+        asm("mov.b64 {%0, %1}, %2;" : "=f"(acc[i][2 * q]), "=f"(acc[i][2 * q + 1]) : "l"(accp[i][q]));
+  }
+
+  // epilogue: f32(addend + acc), f32(+ bias), activation.  The addend may
+  // be the output itself (the SAGE pair), so the compiler cannot move its
+  // loads above earlier stores: each half of the thread's rows loads all of
+  // its addend values first, then stores.
+  float bv[TN];
+#pragma unroll
+  for (int h = 0; h < TN / 4; h++)
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const uint32_t gn = n0 + h * 64 + tx * 4 + j;
+      bv[h * 4 + j] = (bias && gn < n) ? bias[gn] : 0.0f;
+    }
+#pragma unroll
+  for (int half = 0; half < 2; half++) {
+    float ad[4][TN];
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+      const uint64_t gm = m0 + half * 64 + ty * 4 + r;
+#pragma unroll
+      for (int h = 0; h < TN / 4; h++) {
+        const uint32_t gn = n0 + h * 64 + tx * 4;
+        if (addend && gm < m) {
+          if (V4OUT && gn + 3 < n) {
+            const float4 v = *reinterpret_cast<const float4*>(addend + gm * n + gn);
+            ad[r][h * 4 + 0] = v.x; ad[r][h * 4 + 1] = v.y;
+            ad[r][h * 4 + 2] = v.z; ad[r][h * 4 + 3] = v.w;
+          } else {
+#pragma unroll
+            for (int j = 0; j < 4; j++) ad[r][h * 4 + j] = gn + j < n ? addend[gm * n + gn + j] : 0.0f;
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+      const int i = half * 4 + r;
+      const uint64_t gm = m0 + half * 64 + ty * 4 + r;
+      if (gm >= m) continue;
+#pragma unroll
+      for (int h = 0; h < TN / 4; h++) {
+        const uint32_t gn = n0 + h * 64 + tx * 4;
+        float v[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          float x = acc[i][h * 4 + j];
+          if (addend) x = __fadd_rn(ad[r][h * 4 + j], x);
+          if (bias) x = __fadd_rn(x, bv[h * 4 + j]);
+          v[j] = apply_act(x, act, act_param);
+        }
+        if (V4OUT && gn + 3 < n) {
+          *reinterpret_cast<float4*>(C + gm * n + gn) = make_float4(v[0], v[1], v[2], v[3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; j++)
+            if (gn + j < n) C[gm * n + gn + j] = v[j];
+        }
+      }
+    }
+  }
+}
+
+template <int BN, bool EXACT, bool B16, bool V4OUT>
+int launch_pipe_t(bgnn_ctx* ctx, const float* a, const float* b, uint32_t m, uint32_t k,
+                  uint32_t n, const float* addend, const float* bias, int act, double act_param,
+                  float* out) {
+  constexpr size_t smem = pg_smem_bytes<BN>();
+  auto kern = k_sgemm_pipe<BN, EXACT, B16, V4OUT>;
+  BGNN_CUDA(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)smem));
+  dim3 grid((unsigned)((m + PG_BM - 1) / PG_BM), (n + BN - 1) / BN);
+  kern<<<grid, 256, smem, ctx->stream>>>(a, b, m, k, n, addend, bias, act, act_param, out);
+  BGNN_LAUNCHED(ctx);
+  return BGNN_OK;
+}
+
+// out = act(f32(f32(addend + a*b) + bias)), addend / bias optional
+template <bool EXACT>
+int launch_pipe(bgnn_ctx* ctx, const float* a, const float* b, uint32_t m, uint32_t k,
+                uint32_t n, const float* addend, const float* bias, int act, double act_param,
+                float* out) {
+  const bool b16 = (n % 4 == 0) && ((uintptr_t)b % 16 == 0);
+  const bool v4 = (n % 4 == 0) && ((uintptr_t)out % 16 == 0) &&
+                  (addend == nullptr || (uintptr_t)addend % 16 == 0);
+  if (n <= 64) {
+    if (b16)
+      return v4 ? launch_pipe_t<64, EXACT, true, true>(ctx, a, b, m, k, n, addend, bias, act,
+                                                       act_param, out)
+                : launch_pipe_t<64, EXACT, true, false>(ctx, a, b, m, k, n, addend, bias, act,
+                                                        act_param, out);
+    return launch_pipe_t<64, EXACT, false, false>(ctx, a, b, m, k, n, addend, bias, act,
+                                                  act_param, out);
+  }
+  if (b16)
+    return v4 ? launch_pipe_t<128, EXACT, true, true>(ctx, a, b, m, k, n, addend, bias, act,
+                                                      act_param, out)
+              : launch_pipe_t<128, EXACT, true, false>(ctx, a, b, m, k, n, addend, bias, act,
+                                                       act_param, out);
+  return launch_pipe_t<128, EXACT, false, false>(ctx, a, b, m, k, n, addend, bias, act, act_param,
+                                                 out);
+}
+
 template <bool EXACT, bool DUAL>
 int pick_tile(bgnn_ctx* ctx, const GemmArgs& g) {
   if (g.n <= 16) return launch_gemm<256, 16, 4, 4, EXACT, DUAL>(ctx, g);
@@ -385,6 +661,18 @@ int bgnn_run_linear(bgnn_ctx* ctx, const float* a, const float* w, const float* 
   GemmArgs g{a, w, a2, w2, bias, out, m, k, n, act, act_param};
   const bool dual = a2 != nullptr && w2 != nullptr;
   const bool exact = ctx->math == BGNN_MATH_EXACT;
+  constexpr bool kPipeWide = true, kPipeNarrow = true;
+  if ((n > 64 && kPipeWide) || (n <= 64 && kPipeNarrow)) {
+    // St = a2*w2 stored as f32, then f32(St + a*w) (+ bias, activation)
+    if (dual) {
+      BGNN_TRY(exact ? launch_pipe<true>(ctx, a2, w2, m, k, n, nullptr, nullptr, 0, 0.0, out)
+                     : launch_pipe<false>(ctx, a2, w2, m, k, n, nullptr, nullptr, 0, 0.0, out));
+    }
+    return exact ? launch_pipe<true>(ctx, a, w, m, k, n, dual ? out : nullptr, bias, act,
+                                     act_param, out)
+                 : launch_pipe<false>(ctx, a, w, m, k, n, dual ? out : nullptr, bias, act,
+                                      act_param, out);
+  }
   if (n > 64) {
     // wide outputs: the 128x128 kernel; the SAGE pair runs as two launches,
     // St = a2*w2 stored as f32 (the reference's Tensor), then f32(St + a*w)
@@ -400,8 +688,9 @@ int bgnn_run_linear_add(bgnn_ctx* ctx, const float* a, const float* w, uint32_t 
                         uint32_t n, const float* addend, const float* bias, int act,
                         double act_param, float* out) {
   if (m == 0 || n == 0) return BGNN_OK;
-  return launch_sgemm128(ctx, a, w, m, k, n, addend, bias, act, act_param, out,
-                         ctx->math == BGNN_MATH_EXACT);
+  return ctx->math == BGNN_MATH_EXACT
+             ? launch_pipe<true>(ctx, a, w, m, k, n, addend, bias, act, act_param, out)
+             : launch_pipe<false>(ctx, a, w, m, k, n, addend, bias, act, act_param, out);
 }
 
 int bgnn_run_activation(bgnn_ctx* ctx, int act, double param, const float* x, uint64_t n,
