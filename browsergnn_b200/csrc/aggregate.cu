@@ -310,7 +310,8 @@ __device__ __forceinline__ void pipe_bar(int id, int count) {
 // how a stage's source rows reach shared memory.  (One bulk copy per edge
 // through the TMA engine, completing on an mbarrier, measured slower at every
 // width: 14.0 vs 13.4 ms at F = 256, 8.0 vs 7.1 ms at F = 100, 18.6 vs
-// 17.3 ms for the F = 32 SpMM.)
+// 17.3 ms for the F = 32 SpMM.  A bulk L2 prefetch per row four stages
+// ahead of the copies was slower still: 18.8 vs 13.9 ms at F = 256.)
 enum : int {
   CP_A16 = 0,  // 16-byte cp.async copies spread over the pipe
   CP_A4 = 1,   // 4-byte cp.async copies (rows not 16-byte aligned)
@@ -330,7 +331,6 @@ __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint
     for (uint32_t i = ptid; i < nrows; i += tp) rdv[i] = a.dinv[rb + i];
 
   const uint32_t nst = (ne + eps - 1) / eps;
-  const uint32_t row_bytes = (uint32_t)fw * 4u;
   // Source ids: sidx slot m % (S+1) holds stage m's ids.  Stages 0..S-2 are
   // loaded before the ring starts; issue(m) fetches stage m+S-1's ids with
   // cp.async in the same group as stage m's rows.  issue(m+S-1) runs at

@@ -6,28 +6,16 @@
 // order: each output is owned by one thread that walks k ascending.
 //   BGNN_MATH_EXACT: f64 fma (the product of two floats is exact in double)
 //                    then one rounding to f32 -- the reference's bits.
-//   BGNN_MATH_FAST:  f32 fma in the same order; differs from the reference
-//                    only where its double result lands on an f32 tie.
+//   BGNN_MATH_FAST:  f32 fma in the same order (packed two per instruction);
+//                    differs from the reference only where its double result
+//                    lands on an f32 tie.
 // K tails are not zero-padded (an extra fma with 0 could turn a -0 into +0).
 // SAGE stores f32(self + neigh) (Tensor.add -> wasmAdd, sage.ts:178-183):
-// narrow outputs accumulate both products in one pass; wide outputs run the
-// 128x128 kernel twice, storing St = X*W_self as f32 (as the reference's
+// the kernel runs twice, storing St = X*W_self as f32 (as the reference's
 // Tensor does) and adding it in the second launch's epilogue.
 #include "bgnn_internal.cuh"
 
 namespace {
-
-struct GemmArgs {
-  const float* a;   // [m, k]
-  const float* b;   // [k, n]
-  const float* a2;  // second product (SAGE), same shapes
-  const float* b2;
-  const float* bias;
-  float* out;       // [m, n]
-  uint32_t m, k, n;
-  int act;
-  double act_param;
-};
 
 template <bool EXACT>
 __device__ __forceinline__ float mac(float a, float b, float acc) {
@@ -38,255 +26,11 @@ __device__ __forceinline__ float mac(float a, float b, float acc) {
   }
 }
 
-template <int BM, int BN, int TM, int TN, bool EXACT, bool DUAL>
-__global__ void __launch_bounds__(256) k_gemm(const GemmArgs g) {
-  constexpr int BK = 8;
-  constexpr int TX = BN / TN;
-  static_assert((BM / TM) * (BN / TN) == 256, "256 threads per tile");
-  constexpr int A_PER = BM * BK / 256;
-  constexpr int B_PER = (BK * BN + 255) / 256;
-  constexpr int NA = DUAL ? 2 : 1;
-  __shared__ __align__(16) float As[NA][2][BK][BM];
-  __shared__ __align__(16) float Bs[NA][2][BK][BN];
-  const int tid = threadIdx.x;
-  const int tx = tid % TX, ty = tid / TX;
-  const uint64_t m0 = (uint64_t)blockIdx.x * BM;
-  const uint32_t n0 = blockIdx.y * BN;
-  const float* A[2] = {g.a, g.a2};
-  const float* B[2] = {g.b, g.b2};
-
-  float acc[NA][TM][TN];
-#pragma unroll
-  for (int p = 0; p < NA; p++)
-#pragma unroll
-    for (int i = 0; i < TM; i++)
-#pragma unroll
-      for (int j = 0; j < TN; j++) acc[p][i][j] = 0.0f;
-
-  float ra[NA][A_PER], rb[NA][B_PER];
-  auto load_tile = [&](uint32_t k0) {
-#pragma unroll
-    for (int p = 0; p < NA; p++) {
-#pragma unroll
-      for (int i = 0; i < A_PER; i++) {
-        const int idx = tid + i * 256;
-        const int r = idx / BK, kk = idx % BK;
-        const uint64_t gm = m0 + r;
-        const uint32_t gk = k0 + kk;
-        ra[p][i] = (gm < g.m && gk < g.k) ? __ldg(A[p] + gm * g.k + gk) : 0.0f;
-      }
-#pragma unroll
-      for (int i = 0; i < B_PER; i++) {
-        const int idx = tid + i * 256;
-        const int kk = idx / BN, c = idx % BN;
-        const uint32_t gk = k0 + kk, gn = n0 + c;
-        rb[p][i] = (idx < BK * BN && gk < g.k && gn < g.n) ? __ldg(B[p] + (uint64_t)gk * g.n + gn)
-                                                            : 0.0f;
-      }
-    }
-  };
-  auto store_tile = [&](int buf) {
-#pragma unroll
-    for (int p = 0; p < NA; p++) {
-#pragma unroll
-      for (int i = 0; i < A_PER; i++) {
-        const int idx = tid + i * 256;
-        As[p][buf][idx % BK][idx / BK] = ra[p][i];
-      }
-#pragma unroll
-      for (int i = 0; i < B_PER; i++) {
-        const int idx = tid + i * 256;
-        if (idx < BK * BN) Bs[p][buf][idx / BN][idx % BN] = rb[p][i];
-      }
-    }
-  };
-
-  const uint32_t ntiles = (g.k + BK - 1) / BK;
-  load_tile(0);
-  store_tile(0);
-  __syncthreads();
-  for (uint32_t t = 0; t < ntiles; t++) {
-    const int cur = t & 1;
-    if (t + 1 < ntiles) load_tile((t + 1) * BK);
-    const int kmax = (int)min((uint32_t)BK, g.k - t * BK);
-#pragma unroll
-    for (int kk = 0; kk < BK; kk++) {
-      if (kk < kmax) {
-#pragma unroll
-        for (int p = 0; p < NA; p++) {
-          float av[TM], bv[TN];
-#pragma unroll
-          for (int i = 0; i < TM; i++) av[i] = As[p][cur][kk][ty * TM + i];
-#pragma unroll
-          for (int j = 0; j < TN; j++) bv[j] = Bs[p][cur][kk][tx * TN + j];
-#pragma unroll
-          for (int i = 0; i < TM; i++)
-#pragma unroll
-            for (int j = 0; j < TN; j++) acc[p][i][j] = mac<EXACT>(av[i], bv[j], acc[p][i][j]);
-        }
-      }
-    }
-    if (t + 1 < ntiles) store_tile(cur ^ 1);
-    __syncthreads();
-  }
-#pragma unroll
-  for (int i = 0; i < TM; i++) {
-    const uint64_t gm = m0 + ty * TM + i;
-    if (gm >= g.m) continue;
-#pragma unroll
-    for (int j = 0; j < TN; j++) {
-      const uint32_t gn = n0 + tx * TN + j;
-      if (gn >= g.n) continue;
-      float v = acc[0][i][j];
-      if constexpr (DUAL) v = __fadd_rn(acc[1][i][j], acc[0][i][j]);
-      if (g.bias) v = __fadd_rn(v, g.bias[gn]);
-      g.out[gm * g.n + gn] = apply_act(v, g.act, g.act_param);
-    }
-  }
-}
-
 // ---------------------------------------------------------------------------
-// 128x128 tile, 8x8 outputs per thread (rows ty*4+{0..3} and 64+ty*4+{0..3},
-// columns tx*4+{0..3} and 64+tx*4+{0..3}): four 16-byte shared loads feed 64
-// FMAs per k step.  Optional addend matrix (SAGE: f32(St + acc)) in the
-// epilogue.  Same k-ascending order per output as wasmMatmul.
-// ---------------------------------------------------------------------------
-template <bool EXACT>
-__global__ void __launch_bounds__(256, 2) k_sgemm128(const float* __restrict__ A,
-                                                     const float* __restrict__ B, uint32_t m,
-                                                     uint32_t k, uint32_t n, const float* addend,
-                                                     const float* __restrict__ bias, int act,
-                                                     double act_param, float* C, int vec) {
-  constexpr int BM = 128, BN = 128, BK = 16;
-  __shared__ __align__(16) float As[2][BK][BM];
-  __shared__ __align__(16) float Bs[2][BK][BN];
-  const int tid = threadIdx.x;
-  const int tx = tid & 15, ty = tid >> 4;
-  const uint64_t m0 = (uint64_t)blockIdx.x * BM;
-  const uint32_t n0 = blockIdx.y * BN;
-  // loads: A row a_r (consecutive threads, conflict-free transposed stores),
-  // k offset a_k..a_k+7;  B row b_k, columns b_n..b_n+7
-  const int a_r = tid & 127, a_k = (tid >> 7) * 8;
-  const int b_k = tid >> 4, b_n = (tid & 15) * 8;
-  const uint64_t gm_a = m0 + a_r;
-  float ra[8], rb[8];
-  auto load = [&](uint32_t k0) {
-    if ((vec & 1) && gm_a < m && k0 + a_k + 7 < k) {
-      const float4* p = reinterpret_cast<const float4*>(A + gm_a * k + k0 + a_k);
-      const float4 v0 = __ldg(p), v1 = __ldg(p + 1);
-      ra[0] = v0.x; ra[1] = v0.y; ra[2] = v0.z; ra[3] = v0.w;
-      ra[4] = v1.x; ra[5] = v1.y; ra[6] = v1.z; ra[7] = v1.w;
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; i++) {
-        const uint32_t gk = k0 + a_k + i;
-        ra[i] = (gm_a < m && gk < k) ? __ldg(A + gm_a * k + gk) : 0.0f;
-      }
-    }
-    const uint32_t gk = k0 + b_k;
-    if ((vec & 2) && gk < k && n0 + b_n + 7 < n) {
-      const float4* p = reinterpret_cast<const float4*>(B + (uint64_t)gk * n + n0 + b_n);
-      const float4 v0 = __ldg(p), v1 = __ldg(p + 1);
-      rb[0] = v0.x; rb[1] = v0.y; rb[2] = v0.z; rb[3] = v0.w;
-      rb[4] = v1.x; rb[5] = v1.y; rb[6] = v1.z; rb[7] = v1.w;
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; i++) {
-        const uint32_t gn = n0 + b_n + i;
-        rb[i] = (gk < k && gn < n) ? __ldg(B + (uint64_t)gk * n + gn) : 0.0f;
-      }
-    }
-  };
-  auto store = [&](int buf) {
-#pragma unroll
-    for (int i = 0; i < 8; i++) As[buf][a_k + i][a_r] = ra[i];
-    *reinterpret_cast<float4*>(&Bs[buf][b_k][b_n]) = make_float4(rb[0], rb[1], rb[2], rb[3]);
-    *reinterpret_cast<float4*>(&Bs[buf][b_k][b_n + 4]) = make_float4(rb[4], rb[5], rb[6], rb[7]);
-  };
-  float acc[8][8];
-#pragma unroll
-  for (int i = 0; i < 8; i++)
-#pragma unroll
-    for (int j = 0; j < 8; j++) acc[i][j] = 0.0f;
-  auto kstep = [&](int cur, int kk) {
-    const float4 a0 = *reinterpret_cast<const float4*>(&As[cur][kk][ty * 4]);
-    const float4 a1 = *reinterpret_cast<const float4*>(&As[cur][kk][64 + ty * 4]);
-    const float4 b0 = *reinterpret_cast<const float4*>(&Bs[cur][kk][tx * 4]);
-    const float4 b1 = *reinterpret_cast<const float4*>(&Bs[cur][kk][64 + tx * 4]);
-    const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-    const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-#pragma unroll
-    for (int i = 0; i < 8; i++)
-#pragma unroll
-      for (int j = 0; j < 8; j++) acc[i][j] = mac<EXACT>(av[i], bv[j], acc[i][j]);
-  };
-
-  const uint32_t ntiles = (k + BK - 1) / BK;
-  if (ntiles > 0) {
-    load(0);
-    store(0);
-    __syncthreads();
-  }
-  // full tiles: no k bound checks in the inner loop
-  const uint32_t nfull = k / BK;
-  uint32_t t = 0;
-  for (; t < nfull; t++) {
-    const int cur = t & 1;
-    if (t + 1 < ntiles) load((t + 1) * BK);
-#pragma unroll
-    for (int kk = 0; kk < BK; kk++) kstep(cur, kk);
-    if (t + 1 < ntiles) store(cur ^ 1);
-    __syncthreads();
-  }
-  if (t < ntiles) {  // the partial last tile (never zero-padded: no extra fma steps)
-    const int cur = t & 1;
-    const int kmax = (int)(k - t * BK);
-    for (int kk = 0; kk < kmax; kk++) kstep(cur, kk);
-  }
-#pragma unroll
-  for (int i = 0; i < 8; i++) {
-    const uint64_t gm = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
-    if (gm >= m) continue;
-#pragma unroll
-    for (int j = 0; j < 8; j++) {
-      const uint32_t gn = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + (j - 4));
-      if (gn >= n) continue;
-      float v = acc[i][j];
-      if (addend) v = __fadd_rn(addend[gm * n + gn], v);
-      if (bias) v = __fadd_rn(v, bias[gn]);
-      C[gm * n + gn] = apply_act(v, act, act_param);
-    }
-  }
-}
-
-template <int BM, int BN, int TM, int TN, bool EXACT, bool DUAL>
-int launch_gemm(bgnn_ctx* ctx, const GemmArgs& g) {
-  dim3 grid((unsigned)((g.m + BM - 1) / BM), (g.n + BN - 1) / BN);
-  k_gemm<BM, BN, TM, TN, EXACT, DUAL><<<grid, 256, 0, ctx->stream>>>(g);
-  BGNN_LAUNCHED(ctx);
-  return BGNN_OK;
-}
-
-int launch_sgemm128(bgnn_ctx* ctx, const float* a, const float* b, uint32_t m, uint32_t k,
-                    uint32_t n, const float* addend, const float* bias, int act, double act_param,
-                    float* out, bool exact) {
-  const int vec = (((k & 3) == 0 && (uintptr_t)a % 16 == 0) ? 1 : 0) |
-                  (((n & 3) == 0 && (uintptr_t)b % 16 == 0) ? 2 : 0);
-  dim3 grid((unsigned)((m + 127) / 128), (n + 127) / 128);
-  if (exact)
-    k_sgemm128<true><<<grid, 256, 0, ctx->stream>>>(a, b, m, k, n, addend, bias, act, act_param,
-                                                    out, vec);
-  else
-    k_sgemm128<false><<<grid, 256, 0, ctx->stream>>>(a, b, m, k, n, addend, bias, act, act_param,
-                                                     out, vec);
-  BGNN_LAUNCHED(ctx);
-  return BGNN_OK;
-}
-
-// ---------------------------------------------------------------------------
-// Multistage X*W: the same per-output k-ascending chain as k_sgemm128, with
-// both operands moved by cp.async into a 4-stage shared-memory ring so no
-// register staging or shared stores sit in the FMA stream.
+// X*W: each output is one k-ascending chain owned by one thread (the
+// reference's order), both operands moved by cp.async into a 4-stage
+// shared-memory ring so no register staging or shared stores sit in the FMA
+// stream.
 //   A [m, k] row-major goes in transposed (As[k][m]) with 4-byte copies:
 //     consecutive threads read consecutive k of one row (coalesced), and
 //     the thread's 8 rows for one k come back as two 16-byte shared loads.
@@ -559,12 +303,6 @@ int launch_pipe(bgnn_ctx* ctx, const float* a, const float* b, uint32_t m, uint3
                                                  out);
 }
 
-template <bool EXACT, bool DUAL>
-int pick_tile(bgnn_ctx* ctx, const GemmArgs& g) {
-  if (g.n <= 16) return launch_gemm<256, 16, 4, 4, EXACT, DUAL>(ctx, g);
-  return launch_gemm<128, 64, 8, 4, EXACT, DUAL>(ctx, g);
-}
-
 // ---- elementwise -----------------------------------------------------------
 __global__ void k_act(int act, double p, const float* __restrict__ x, uint64_t n,
                       float* __restrict__ out) {
@@ -658,30 +396,17 @@ int bgnn_run_linear(bgnn_ctx* ctx, const float* a, const float* w, const float* 
                     int act, double act_param, float* out) {
   if (m == 0 || n == 0) return BGNN_OK;
   // k == 0 runs no mac step: the output is act(0 + bias), as in the reference
-  GemmArgs g{a, w, a2, w2, bias, out, m, k, n, act, act_param};
   const bool dual = a2 != nullptr && w2 != nullptr;
   const bool exact = ctx->math == BGNN_MATH_EXACT;
-  constexpr bool kPipeWide = true, kPipeNarrow = true;
-  if ((n > 64 && kPipeWide) || (n <= 64 && kPipeNarrow)) {
-    // St = a2*w2 stored as f32, then f32(St + a*w) (+ bias, activation)
-    if (dual) {
-      BGNN_TRY(exact ? launch_pipe<true>(ctx, a2, w2, m, k, n, nullptr, nullptr, 0, 0.0, out)
-                     : launch_pipe<false>(ctx, a2, w2, m, k, n, nullptr, nullptr, 0, 0.0, out));
-    }
-    return exact ? launch_pipe<true>(ctx, a, w, m, k, n, dual ? out : nullptr, bias, act,
-                                     act_param, out)
-                 : launch_pipe<false>(ctx, a, w, m, k, n, dual ? out : nullptr, bias, act,
-                                      act_param, out);
+  // SAGE pair: St = a2*w2 stored as f32 (the reference's Tensor), then
+  // f32(St + a*w) (+ bias, activation) in the second launch's epilogue
+  if (dual) {
+    BGNN_TRY(exact ? launch_pipe<true>(ctx, a2, w2, m, k, n, nullptr, nullptr, 0, 0.0, out)
+                   : launch_pipe<false>(ctx, a2, w2, m, k, n, nullptr, nullptr, 0, 0.0, out));
   }
-  if (n > 64) {
-    // wide outputs: the 128x128 kernel; the SAGE pair runs as two launches,
-    // St = a2*w2 stored as f32 (the reference's Tensor), then f32(St + a*w)
-    if (dual) BGNN_TRY(launch_sgemm128(ctx, a2, w2, m, k, n, nullptr, nullptr, 0, 0.0, out, exact));
-    return launch_sgemm128(ctx, a, w, m, k, n, dual ? out : nullptr, bias, act, act_param, out,
-                           exact);
-  }
-  if (exact) return dual ? pick_tile<true, true>(ctx, g) : pick_tile<true, false>(ctx, g);
-  return dual ? pick_tile<false, true>(ctx, g) : pick_tile<false, false>(ctx, g);
+  const float* addend = dual ? out : nullptr;
+  return exact ? launch_pipe<true>(ctx, a, w, m, k, n, addend, bias, act, act_param, out)
+               : launch_pipe<false>(ctx, a, w, m, k, n, addend, bias, act, act_param, out);
 }
 
 int bgnn_run_linear_add(bgnn_ctx* ctx, const float* a, const float* w, uint32_t m, uint32_t k,
