@@ -344,26 +344,41 @@ __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint
   // Row slices move as cp.async copies of 16 (CP_A16) or 4 bytes spread over
   // the pipe, consecutive threads on consecutive chunks of one row; per-edge
   // weights (GCN dinv, SpMM values) as 4-byte cp.async by the edge's thread.
+  // Copy c of a stage (c = ptid, ptid + tp, ...) is chunk q = c % ch of
+  // edge j = c / ch; the thread walks (j, q) incrementally (ch <= tp always),
+  // so the copy loop has no integer division.
+  const int ch = CP == CP_A16 ? fw >> 2 : fw;  // chunks per edge (16 or 4 bytes)
+  const int cdj = tp / ch, cdq = tp - cdj * ch;
+  const int cj0 = ptid / ch, cq0 = ptid - cj0 * ch;
   auto issue = [&](uint32_t k) {
     if (k < nst) {
       const int slot = (int)((kg + k) % ST_S);
       const uint32_t* sid = sidx + (k % (ST_S + 1)) * eps;
       const int cnt = (int)min((uint32_t)eps, ne - k * (uint32_t)eps);  // edges in this stage
       float* sb = buf + (size_t)slot * eps * swp;
-      if (CP == CP_A16) {
-        const int ch = fw >> 2;  // 16-byte chunks per edge (fw is a multiple of 4 here)
-        const int copies = cnt * ch;
-        for (int c = ptid; c < copies; c += tp) {
-          const int j = c / ch;
-          const int q = c - j * ch;
-          cp_async16(sb + (size_t)j * swp + 4 * q, a.x + (int64_t)sid[j] * a.ld_x + f0 + 4 * q);
+      constexpr int QB = CP == CP_A16 ? 4 : 1;  // floats per chunk
+      if (cdq == 0) {
+        // ch divides the pipe width: the thread's chunk q never changes
+        const float* src = a.x + f0 + QB * cq0;
+        float* dst = sb + QB * cq0;
+        for (int j = cj0; j < cnt; j += cdj) {
+          if (CP == CP_A16)
+            cp_async16(dst + (size_t)j * swp, src + (int64_t)sid[j] * a.ld_x);
+          else
+            cp_async4(dst + (size_t)j * swp, src + (int64_t)sid[j] * a.ld_x);
         }
       } else {
-        const int copies = cnt * fw;
-        for (int c = ptid; c < copies; c += tp) {
-          const int j = c / fw;
-          const int q = c - j * fw;
-          cp_async4(sb + (size_t)j * swp + q, a.x + (int64_t)sid[j] * a.ld_x + f0 + q);
+        int j = cj0, q = cq0;
+        for (; j < cnt; j += cdj) {
+          if (CP == CP_A16)
+            cp_async16(sb + (size_t)j * swp + 4 * q, a.x + (int64_t)sid[j] * a.ld_x + f0 + 4 * q);
+          else
+            cp_async4(sb + (size_t)j * swp + q, a.x + (int64_t)sid[j] * a.ld_x + f0 + q);
+          q += cdq;
+          if (q >= ch) {
+            q -= ch;
+            j++;
+          }
         }
       }
       if (ptid < cnt) {
