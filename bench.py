@@ -215,6 +215,8 @@ class PartitionedSage:
         self.st = [torch.empty((n_own, lay.outChannels), dtype=torch.float32, device=dev)
                    for lay in layers]
         self.out = torch.empty((n_own, layers[-1].outChannels), dtype=torch.float32, device=dev)
+        self.send = [torch.empty((part.n_send, lay.inChannels), dtype=torch.float32, device=dev)
+                     for lay in layers]
         self.side = torch.cuda.Stream(device=dev)
         from browsergnn_b200.partition import cuda_pack
 
@@ -243,14 +245,16 @@ class PartitionedSage:
             out = self.ext[li + 1][:n_own] if li + 1 < nl else self.out
             act = 1 if li < nl - 1 else 0
             split = fout > 64
+            e0 = mark()
+            # pack the rows the other ranks need, then start x * W_self (owned
+            # rows only) on the side stream while the rows are exchanged
+            part.pack_send(ext, self.pack, self.send[li])
             if split:
-                # x * W_self needs only the owned rows: start it before the exchange
                 self.side.wait_stream(main)
                 with torch.cuda.stream(self.side):
                     ctx.call("bgnn_linear", ptr(ext), ptr(lay.p("lin_self")), n_own, fin, fout,
                              None, 0, 0.0, ptr(self.st[li]))
-            e0 = mark()
-            part.exchange_into(ext, self.pack)
+            part.send_recv(ext, self.send[li])
             e1 = mark()
             ctx.call("bgnn_aggregate", dg.h, 1, ptr(ext), fin, ptr(agg))
             e2 = mark()
@@ -608,8 +612,15 @@ def main():
     if world > 1:
         import datetime
 
+        opts = None
+        try:  # NCCL kernels on a high-priority stream: the halo exchange runs
+            # next to the side-stream GEMM instead of queueing behind its CTAs
+            opts = dist.ProcessGroupNCCL.Options()
+            opts.is_high_priority_stream = True
+        except Exception:  # noqa: BLE001 - older builds: default stream priority
+            opts = None
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device(f"cuda:{local}"))
+                                device_id=torch.device(f"cuda:{local}"), pg_options=opts)
     bg.init_browsergnn({"device": local})
     ctx = bg.get_context(local)
     hbm_peak, peak_kind = peaks()

@@ -317,7 +317,7 @@ enum : int {
   CP_A4 = 1,   // 4-byte cp.async copies (rows not 16-byte aligned)
 };
 
-template <int OP, int CP>
+template <int OP, int CP, int S = ST_S, bool ONE_ROW = false>
 __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint32_t re, int f0,
                                              int fw, int swp, int tp, int ptid, int eps,
                                              float* buf, float* wbuf, uint32_t* sidx, uint32_t* rps,
@@ -339,7 +339,7 @@ __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint
   auto fetch_ids = [&](uint32_t m) {
     const uint32_t e = m * (uint32_t)eps + (uint32_t)ptid;
     if (ptid < eps && m < nst && e < ne)
-      cp_async4(sidx + (m % (ST_S + 1)) * eps + ptid, a.src_of + e0 + e);
+      cp_async4(sidx + (m % (S + 1)) * eps + ptid, a.src_of + e0 + e);
   };
   // Row slices move as cp.async copies of 16 (CP_A16) or 4 bytes spread over
   // the pipe, consecutive threads on consecutive chunks of one row; per-edge
@@ -352,8 +352,8 @@ __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint
   const int cj0 = ptid / ch, cq0 = ptid - cj0 * ch;
   auto issue = [&](uint32_t k) {
     if (k < nst) {
-      const int slot = (int)((kg + k) % ST_S);
-      const uint32_t* sid = sidx + (k % (ST_S + 1)) * eps;
+      const int slot = (int)((kg + k) % S);
+      const uint32_t* sid = sidx + (k % (S + 1)) * eps;
       const int cnt = (int)min((uint32_t)eps, ne - k * (uint32_t)eps);  // edges in this stage
       float* sb = buf + (size_t)slot * eps * swp;
       constexpr int QB = CP == CP_A16 ? 4 : 1;  // floats per chunk
@@ -387,20 +387,20 @@ __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint
         if (OP == OP_SPMM || OP == OP_SPMM_X) cp_async4(w, a.val + e0 + k * (uint32_t)eps + ptid);
       }
     }
-    fetch_ids(k + ST_S - 1);
+    fetch_ids(k + S - 1);
     cp_async_commit();
   };
 
   if (ptid < eps) {
 #pragma unroll
-    for (uint32_t m = 0; m < ST_S - 1; m++) {
+    for (uint32_t m = 0; m < S - 1; m++) {
       const uint32_t e = m * (uint32_t)eps + (uint32_t)ptid;
       if (m < nst && e < ne) sidx[m * eps + ptid] = a.src_of[e0 + e];
     }
   }
   pipe_bar(bar_id, tp);
 #pragma unroll
-  for (int k = 0; k < ST_S - 1; k++) issue((uint32_t)k);
+  for (int k = 0; k < S - 1; k++) issue((uint32_t)k);
   const bool consumer = ptid < fw;
   float acc = init_acc<OP>();
   uint32_t r = 0;
@@ -418,11 +418,49 @@ __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint
     }
   };
   for (uint32_t k = 0; k < nst; k++) {
-    const int slot = (int)((kg + k) % ST_S);
-    cp_async_wait<ST_S - 2>();  // this thread's copies of stage k have landed
+    const int slot = (int)((kg + k) % S);
+    cp_async_wait<S - 2>();  // this thread's copies of stage k have landed
     pipe_bar(bar_id, tp);       // ... and everyone's; stage k-1's slot is free
-    issue(k + ST_S - 1);
-    if (consumer) {
+    issue(k + S - 1);
+    if (ONE_ROW && consumer) {
+      // a single row (a giant slice): no row ends inside the stream, and the
+      // add chain is the critical path, so the shared-memory reads run R
+      // edges ahead of the adds in a rolling register window
+      const float* b = buf + (size_t)slot * eps * swp + ptid;
+      const float* wb = wbuf + slot * eps;
+      const uint32_t cnt = min((uint32_t)eps, ne - k * (uint32_t)eps);
+      constexpr int R = 16;
+      constexpr bool HAS_W = OP == OP_GCN || OP == OP_SPMM || OP == OP_SPMM_X;
+      float v[R], wr[R];
+#pragma unroll
+      for (int u = 0; u < R; u++) {
+        v[u] = (uint32_t)u < cnt ? b[(size_t)u * swp] : 0.0f;
+        wr[u] = (HAS_W && (uint32_t)u < cnt) ? wb[u] : 0.0f;
+      }
+      uint32_t j = 0;
+      for (; j + 2 * R <= cnt; j += R) {
+#pragma unroll
+        for (int u = 0; u < R; u++) {
+          const float w = (OP == OP_GCN) ? __fmul_rn(wr[u], dinv_r) : wr[u];
+          acc = step<OP>(acc, v[u], w);
+          v[u] = b[(size_t)(j + R + u) * swp];
+          if (HAS_W) wr[u] = wb[j + R + u];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < R; u++) {  // the window's last R (or fewer) edges
+        if (j + u < cnt) {
+          const float w = (OP == OP_GCN) ? __fmul_rn(wr[u], dinv_r) : wr[u];
+          acc = step<OP>(acc, v[u], w);
+        }
+      }
+      for (j += R; j < cnt; j++) {
+        float w = 0.0f;
+        if (OP == OP_GCN) w = __fmul_rn(wb[j], dinv_r);
+        if (OP == OP_SPMM || OP == OP_SPMM_X) w = wb[j];
+        acc = step<OP>(acc, b[(size_t)j * swp], w);
+      }
+    } else if (consumer) {
       const float* b = buf + (size_t)slot * eps * swp + ptid;
       const float* wb = wbuf + slot * eps;
       const uint32_t base = k * (uint32_t)eps;
@@ -471,7 +509,7 @@ __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint
 template <int OP, bool A16>
 __global__ void __launch_bounds__(ST_THREADS, 2)
     k_agg_stream(const AggArgs a, int P, int swp, int n_slices, uint32_t n_giant, int gsw,
-                 int eps_g, uint32_t* queue) {
+                 int eps_g, int mode, uint32_t n_ex, uint32_t* queue) {
   extern __shared__ float4 st_smem4[];
   float* data = reinterpret_cast<float*>(st_smem4);
   const size_t data_f = stream_data_floats(P, swp);
@@ -490,13 +528,16 @@ __global__ void __launch_bounds__(ST_THREADS, 2)
   const int tp = ST_THREADS / P;
   constexpr int CP = A16 ? CP_A16 : CP_A4;  // rows 16-byte aligned: 16-byte copies
 
-  // phase 1: heavy rows with the whole CTA as one pipe.  Giant rows (the
-  // first n_giant heavy items, chosen at launch) are cut into gsw-feature
-  // slices with eps_g edges per stage, so several CTAs stream one hub row at
-  // once; each slice is still reduced in edge order by one thread per feature.
+  // Giant rows (the first n_giant heavy items, chosen at launch) are cut into
+  // gsw-feature slices with eps_g edges per stage, so several CTAs stream one
+  // hub row at once; each slice is still reduced in edge order by one thread
+  // per feature.  mode 2: the slices of the first n_ex giant rows run in
+  // their own launch (k_agg_giant), skip them; mode 0: everything here.
   uint32_t kg = 0;  // stages run so far (ring slot)
+  const uint32_t w0 = mode == 2 ? n_ex * gs : 0u;
+  // phase 1: heavy rows with the whole CTA as one pipe
   for (;;) {
-    if (threadIdx.x == 0) slots[P] = (int)atomicAdd(&queue[0], 1u);
+    if (threadIdx.x == 0) slots[P] = (int)(w0 + atomicAdd(&queue[0], 1u));
     __syncthreads();
     const uint32_t w = (uint32_t)slots[P];
     if (w >= heavy_work) break;
@@ -534,6 +575,36 @@ __global__ void __launch_bounds__(ST_THREADS, 2)
   }
 }
 
+// Giant-row slices in their own launch: one CTA per slice, alone on its SM
+// (its shared memory request leaves no room for a second CTA), with a deeper
+// ring than the shared-SM pipes since the whole SM's shared memory is its.
+constexpr int GS_S = 5;  // ring stages of a giant-slice CTA
+constexpr size_t giant_smem_bytes() {
+  return ((size_t)GS_S * ST_GSTAGE + (size_t)GS_S * ST_THREADS + (size_t)(GS_S + 1) * ST_THREADS +
+          16) * 4;
+}
+
+template <int OP, bool A16>
+__global__ void __launch_bounds__(ST_THREADS, 1)
+    k_agg_giant(const AggArgs a, uint32_t n_ex, int gsw, int eps_g) {
+  extern __shared__ float4 gt_smem4[];
+  float* data = reinterpret_cast<float*>(gt_smem4);
+  float* wb = data + (size_t)GS_S * ST_GSTAGE;
+  uint32_t* sidx = reinterpret_cast<uint32_t*>(wb + GS_S * ST_THREADS);
+  uint32_t* rps = sidx + (GS_S + 1) * ST_THREADS;  // one row per item: 2 offsets
+  float* rdv = reinterpret_cast<float*>(rps + 4);
+  const int F = a.num_features;
+  const uint32_t gs = (uint32_t)((F + gsw - 1) / gsw);
+  constexpr int CP = A16 ? CP_A16 : CP_A4;
+  uint32_t kg = 0;
+  for (uint32_t w = blockIdx.x; w < n_ex * gs; w += gridDim.x) {
+    const uint2 item = a.items[w / gs];
+    const int f0 = (int)(w % gs) * gsw;
+    stream_range<OP, CP, GS_S, true>(a, item.x, item.y, f0, min(gsw, F - f0), gsw, ST_THREADS,
+                                     threadIdx.x, eps_g, data, wb, sidx, rps, rdv, kg, 0);
+  }
+}
+
 template <int OP, bool A16>
 int launch_stream_t(bgnn_ctx* ctx, const AggArgs& a, int P, int swp, int n_slices) {
   size_t smem = (stream_data_floats(P, swp) + stream_w_floats(P) + stream_sidx_words(P) +
@@ -568,9 +639,40 @@ int launch_stream_t(bgnn_ctx* ctx, const AggArgs& a, int P, int swp, int n_slice
   const int eps_g = ST_GSTAGE / gsw;  // edges per giant stage (at most ST_THREADS)
   uint32_t* queue = ctx->d_small;
   BGNN_CUDA(ctx, cudaMemsetAsync(queue, 0, 2 * sizeof(uint32_t), ctx->stream));
+  // rows long enough (four CTA shares or more) to finish last even when cut
+  // into slices get their own launch, up to a quarter of the SMs
+  uint32_t n_ex = 0;
+  if (n_giant > 0) {
+    const double share = (double)a.num_edges * (double)F * 4.0 / (double)grid;
+    const uint32_t gs = (uint32_t)((F + gsw - 1) / gsw);
+    const uint32_t cap = (uint32_t)ctx->num_sms / 4 / gs;
+    while (n_ex < n_giant && n_ex < cap && (double)a.heavy_deg[n_ex] * F * 4.0 > 4.0 * share) n_ex++;
+  }
+  int mode = 0;
+  if (n_ex > 0) {
+    // The giant slices go first, in their own launch on the (high-priority)
+    // aux stream, one CTA per slice with enough shared memory that nothing
+    // else shares its SM: a slice is one serial add chain per feature, and on
+    // a shared SM its single consumer warp gets a fraction of the issue slots
+    // and its two stages in flight leave it waiting on memory.
+    // The main launch skips them; its persistent CTAs that find no room
+    // start as the slices finish and pull from the same work queue.
+    constexpr size_t gsmem = giant_smem_bytes();
+    static_assert(gsmem > 228 * 1024 - 106 * 1024, "a giant-slice CTA must fill its SM");
+    BGNN_CUDA(ctx, cudaFuncSetAttribute(k_agg_giant<OP, A16>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsmem));
+    BGNN_CUDA(ctx, cudaEventRecord(ctx->ev_fork, ctx->stream));
+    BGNN_CUDA(ctx, cudaStreamWaitEvent(ctx->aux_stream, ctx->ev_fork, 0));
+    const uint32_t gs = (uint32_t)((F + gsw - 1) / gsw);
+    k_agg_giant<OP, A16><<<n_ex * gs, ST_THREADS, gsmem, ctx->aux_stream>>>(a, n_ex, gsw, eps_g);
+    BGNN_LAUNCHED(ctx);
+    BGNN_CUDA(ctx, cudaEventRecord(ctx->ev_join, ctx->aux_stream));
+    mode = 2;
+  }
   k_agg_stream<OP, A16><<<(unsigned)grid, ST_THREADS, smem, ctx->stream>>>(
-      a, P, swp, n_slices, n_giant, gsw, eps_g, queue);
+      a, P, swp, n_slices, n_giant, gsw, eps_g, mode, n_ex, queue);
   BGNN_LAUNCHED(ctx);
+  if (n_ex > 0) BGNN_CUDA(ctx, cudaStreamWaitEvent(ctx->stream, ctx->ev_join, 0));
   return BGNN_OK;
 }
 

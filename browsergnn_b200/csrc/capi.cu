@@ -94,7 +94,10 @@ extern "C" int bgnn_ctx_create(int device, bgnn_ctx** out) {
   bool ok = cudaSetDevice(device) == cudaSuccess;
   ok = ok && cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device) == cudaSuccess;
   ok = ok && cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking) == cudaSuccess;
-  ok = ok && cudaStreamCreateWithFlags(&c->aux_stream, cudaStreamNonBlocking) == cudaSuccess;
+  int lo_prio = 0, hi_prio = 0;
+  ok = ok && cudaDeviceGetStreamPriorityRange(&lo_prio, &hi_prio) == cudaSuccess;
+  // the aux stream runs work that gates the main stream (heavy rows, hub slices)
+  ok = ok && cudaStreamCreateWithPriority(&c->aux_stream, cudaStreamNonBlocking, hi_prio) == cudaSuccess;
   ok = ok && cudaEventCreateWithFlags(&c->ev_fork, cudaEventDisableTiming) == cudaSuccess;
   ok = ok && cudaEventCreateWithFlags(&c->ev_join, cudaEventDisableTiming) == cudaSuccess;
   ok = ok && cudaMalloc(&c->d_err, 4 * sizeof(int)) == cudaSuccess;

@@ -101,21 +101,30 @@ class HaloPlan:
                                group=self.group)
         return ext
 
+    def pack_send(self, ext, pack: Callable, send=None):
+        """Gather the rows other ranks asked for from the owned part of ext
+        into a send buffer (allocated unless given)."""
+        torch = _torch()
+        f = int(ext.shape[1])
+        if send is None:
+            send = torch.empty((self.n_send, f), dtype=ext.dtype, device=ext.device)
+        if self.n_send:
+            pack(ext[: self.n_own], self.send_rows, send)
+        return send
+
+    def send_recv(self, ext, send):
+        """All-to-all of packed rows into the halo rows ext[n_own:]."""
+        import torch.distributed as dist
+
+        dist.all_to_all_single(ext[self.n_own:], send, self.recv_splits, self.send_splits,
+                               group=self.group)
+        return ext
+
     def exchange_into(self, ext, pack: Callable):
         """Fill the halo rows ext[n_own:] of a buffer whose owned rows
         ext[:n_own] already hold this rank's features (no copy of the owned
         part)."""
-        import torch.distributed as dist
-
-        torch = _torch()
-        f = int(ext.shape[1])
-        own = ext[: self.n_own]
-        send = torch.empty((self.n_send, f), dtype=ext.dtype, device=ext.device)
-        if self.n_send:
-            pack(own, self.send_rows, send)
-        dist.all_to_all_single(ext[self.n_own:], send, self.recv_splits, self.send_splits,
-                               group=self.group)
-        return ext
+        return self.send_recv(ext, self.pack_send(ext, pack))
 
     def device_graph(self, device: Optional[int] = None):
         from .graph import DeviceGraph
