@@ -114,6 +114,16 @@ class GraphData:
         f = int(cfg["numFeatures"])
         e = int(cfg["numEdges"])
         ei = cfg["edgeIndex"]
+        self._x_ready = None
+        # Pinned host tensors are uploaded without blocking the host: the edge
+        # list first on the current stream (the CSR build needs it), then the
+        # features on a copy stream, so the copy of x overlaps the CSR build;
+        # x_device() makes the consumer's stream wait for it.
+        if _is_pinned_host(ei) and _is_pinned_host(x):
+            torch = _torch()
+            dev = torch.cuda.current_device()
+            ei = ei.to(f"cuda:{dev}", non_blocking=True)
+            x, self._x_ready = _upload_on_copy_stream(x, dev)
         if _is_cuda_tensor(x):
             torch = _torch()
             xlen = x.numel()
@@ -164,6 +174,8 @@ class GraphData:
 
     def x_device(self, device: Optional[int] = None):
         torch = _torch()
+        if self._x_ready is not None:
+            torch.cuda.current_stream().wait_event(self._x_ready)
         if _is_cuda_tensor(self.x) and self.x.dtype == torch.float32:
             return self.x.contiguous()
         dev = self.device_graph(device).device
@@ -201,6 +213,12 @@ class GraphData:
         """graph.ts:220-227 (flag computed during the device CSR build)."""
         return self.device_graph().has_self_loops
 
+    def _x_settled(self):
+        """self.x, with any pending upload ordered before the current stream."""
+        if self._x_ready is not None:
+            _torch().cuda.current_stream().wait_event(self._x_ready)
+        return self.x
+
     def addSelfLoops(self) -> "GraphData":
         """graph.ts:232-272: a loop for every node lacking one, appended after
         the original edges in node order."""
@@ -212,8 +230,9 @@ class GraphData:
         add = np.flatnonzero(~has).astype(np.uint32)
         ne = e + add.size
         new = np.concatenate([src, add, dst, add]).astype(np.uint32)
-        return GraphData(x=self.x, numNodes=n, numFeatures=self.numFeatures, edgeIndex=new,
-                         numEdges=ne, batch=self.batch, y=self.y, graphLabel=self.graphLabel)
+        return GraphData(x=self._x_settled(), numNodes=n, numFeatures=self.numFeatures,
+                         edgeIndex=new, numEdges=ne, batch=self.batch, y=self.y,
+                         graphLabel=self.graphLabel)
 
     def removeSelfLoops(self) -> "GraphData":
         """graph.ts:277-304."""
@@ -221,9 +240,9 @@ class GraphData:
         e = self.numEdges
         keep = ei[:e] != ei[e:]
         new = np.concatenate([ei[:e][keep], ei[e:][keep]])
-        return GraphData(x=self.x, numNodes=self.numNodes, numFeatures=self.numFeatures,
-                         edgeIndex=new, numEdges=int(keep.sum()), batch=self.batch, y=self.y,
-                         graphLabel=self.graphLabel)
+        return GraphData(x=self._x_settled(), numNodes=self.numNodes,
+                         numFeatures=self.numFeatures, edgeIndex=new, numEdges=int(keep.sum()),
+                         batch=self.batch, y=self.y, graphLabel=self.graphLabel)
 
     def withFeatures(self, new_x) -> "GraphData":
         """graph.ts:309-325, sharing the cached device CSR (no revalidation)."""
@@ -233,8 +252,37 @@ class GraphData:
         g = GraphData.__new__(GraphData)
         g.__dict__.update(self.__dict__)
         g.x = new_x
+        g._x_ready = None
         g.numFeatures = int(new_x.shape[1])
         return g
+
+
+def _is_pinned_host(a) -> bool:
+    try:
+        torch = _torch()
+    except Exception:  # pragma: no cover
+        return False
+    return isinstance(a, torch.Tensor) and not a.is_cuda and a.is_pinned()
+
+
+_copy_streams: dict = {}
+
+
+def _upload_on_copy_stream(t, device: int):
+    """Start an asynchronous host->device copy of a pinned tensor on a side
+    stream; returns the device tensor and the event that marks its arrival."""
+    torch = _torch()
+    s = _copy_streams.get(device)
+    if s is None:
+        s = torch.cuda.Stream(device=device)
+        _copy_streams[device] = s
+    s.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(s):
+        d = t.to(f"cuda:{device}", non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(s)
+    d.record_stream(torch.cuda.current_stream(device))
+    return d, ev
 
 
 def _is_cuda_tensor(a) -> bool:

@@ -352,3 +352,24 @@ def test_linear_add_is_sage_linear_split(bg, n):
     comb = (st_o.astype(np.float64) + nt_o).astype(np.float32)
     comb = (comb.astype(np.float64) + b).astype(np.float32)
     assert_bits_equal(out.cpu().numpy(), orc.relu(comb), "vs oracle")
+
+
+def test_pinned_host_graphdata_overlaps_upload(bg):
+    """GraphData from pinned host tensors (edges uploaded first, features on
+    a copy stream) gives the same layer output as from numpy arrays."""
+    import torch
+
+    rng = np.random.default_rng(12)
+    n, f = 3000, 24
+    ei, e = rand_graph(n, 20000, 6, hub_deg=800, loops=3)
+    x = rng.standard_normal((n, f)).astype(np.float32)
+    conv = bg.SAGEConv(inChannels=f, outChannels=16)
+    _inject(bg, conv, rng)
+    want = conv.forward(bg.GraphData(x=x, numNodes=n, numFeatures=f, edgeIndex=ei,
+                                     numEdges=e)).x.cpu().numpy()
+    xh = torch.from_numpy(x).pin_memory()
+    eh = torch.from_numpy(ei.view(np.int32)).pin_memory()
+    g = bg.GraphData(x=xh, numNodes=n, numFeatures=f, edgeIndex=eh, numEdges=e)
+    got = conv.forward(g).x.cpu().numpy()
+    assert_bits_equal(got, want, "pinned-host GraphData")
+    assert g.addSelfLoops().numEdges >= e
