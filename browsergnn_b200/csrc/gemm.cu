@@ -107,7 +107,7 @@ __global__ void __launch_bounds__(256, 2) k_sgemm_pipe(const float* __restrict__
     const uint32_t k0 = t * PG_BK;
 #pragma unroll
     for (int i = 0; i < (PG_BM * PG_BK) / 256; i++) {
-      const int dk = 8 * (i & 1), dr = 32 * (i >> 1);
+      const int dk = 8 * (i % (PG_BK / 8)), dr = 32 * (i / (PG_BK / 8));
       const bool ok = k0 + a_kk + dk < k && m0 + a_r + dr < m;
       cpa4_zfill(a_dst + slot * A_STAGE + dk * AST + dr,
                  ok ? a_src + (uint64_t)dr * k + k0 + dk : A, ok);
@@ -184,14 +184,24 @@ __global__ void __launch_bounds__(256, 2) k_sgemm_pipe(const float* __restrict__
   for (uint32_t t = 0; t < ntiles; t++) {
     cpa_wait<PG_S - 2>();  // this thread's copies of tile t have landed
     __syncthreads();       // ... everyone's; and tile t-1's slot is free
-    if (t + PG_S - 1 < ntiles) load_stage(t + PG_S - 1, (int)((t + PG_S - 1) % PG_S));
-    cpa_commit();
     const int slot = (int)(t % PG_S);
     const float* as = As + slot * A_STAGE;
     const float* bs = Bs + slot * B_STAGE;
     const int kn = (int)min((uint32_t)PG_BK, k - t * PG_BK);  // the last tile may be partial
+    if (kn == PG_BK) {
+      // the next stage's copies go out between the two halves of the tile,
+      // so no warp issues them while the others wait at the barrier
 #pragma unroll PG_UNROLL
-    for (int kk = 0; kk < kn; kk++) kstep(as, bs, kk);
+      for (int kk = 0; kk < PG_BK / 2; kk++) kstep(as, bs, kk);
+      if (t + PG_S - 1 < ntiles) load_stage(t + PG_S - 1, (int)((t + PG_S - 1) % PG_S));
+      cpa_commit();
+#pragma unroll PG_UNROLL
+      for (int kk = PG_BK / 2; kk < PG_BK; kk++) kstep(as, bs, kk);
+    } else {
+      if (t + PG_S - 1 < ntiles) load_stage(t + PG_S - 1, (int)((t + PG_S - 1) % PG_S));
+      cpa_commit();
+      for (int kk = 0; kk < kn; kk++) kstep(as, bs, kk);
+    }
   }
   cpa_wait<0>();
   if constexpr (!EXACT) {
