@@ -201,14 +201,32 @@ class PartitionedSage:
     adds to it (bgnn_linear_add), the same two f32 results and the same final
     rounding as bgnn_sage_linear."""
 
-    def __init__(self, layers, part, dg, x, ctx):
+    def __init__(self, layers, part, dg, x, ctx, peer_stores=True):
         import torch
+
+        from browsergnn_b200.partition import PeerStores, SharedBuffer
 
         self.layers, self.part, self.dg, self.ctx = layers, part, dg, ctx
         n_own, n_ext = part.n_own, part.n_own + part.n_halo
         dev = x.device
-        self.ext = [torch.empty((n_ext, lay.inChannels), dtype=torch.float32, device=dev)
-                    for lay in layers]
+        # Layers 2.. read buffers that the previous layer's epilogue fills,
+        # halo rows included, by storing into the peers' mapped buffers
+        # (bgnn_linear_add_remote); the input features go through the
+        # all-to-all.
+        self.shared = []
+        self.peer = None
+        self.ext = [torch.empty((n_ext, layers[0].inChannels), dtype=torch.float32, device=dev)]
+        for lay in layers[1:]:
+            if peer_stores:
+                b = SharedBuffer(ctx, n_ext, lay.inChannels)
+                self.shared.append(b)
+                self.ext.append(b.tensor)
+            else:
+                self.ext.append(torch.empty((n_ext, lay.inChannels), dtype=torch.float32,
+                                            device=dev))
+        if peer_stores:
+            self.peer = PeerStores(part, ctx, self.shared)
+        self.flag = torch.zeros(1, dtype=torch.float32, device=dev)
         self.ext[0][:n_own].copy_(x)
         self.agg = [torch.empty((n_own, lay.inChannels), dtype=torch.float32, device=dev)
                     for lay in layers]
@@ -222,8 +240,23 @@ class PartitionedSage:
 
         self.pack = cuda_pack(ctx)
 
+    def close(self):
+        """Unmap the peers' buffers everywhere, then free this rank's."""
+        import torch.distributed as dist
+
+        import torch
+
+        torch.cuda.synchronize()
+        if self.peer is not None:
+            self.peer.close()
+        dist.barrier(group=self.part.group)
+        for b in self.shared:
+            b.free()
+        self.shared = []
+
     def forward(self, timers=None):
         import torch
+        import torch.distributed as dist
 
         from browsergnn_b200.backend import ptr
 
@@ -245,20 +278,34 @@ class PartitionedSage:
             out = self.ext[li + 1][:n_own] if li + 1 < nl else self.out
             act = 1 if li < nl - 1 else 0
             split = fout > 64
+            halo_ready = li > 0 and self.peer is not None  # filled by the previous epilogue
+            remote_out = self.peer is not None and li + 1 < nl and split
             e0 = mark()
             # pack the rows the other ranks need, then start x * W_self (owned
             # rows only) on the side stream while the rows are exchanged
-            part.pack_send(ext, self.pack, self.send[li])
+            if not halo_ready:
+                part.pack_send(ext, self.pack, self.send[li])
             if split:
                 self.side.wait_stream(main)
                 with torch.cuda.stream(self.side):
                     ctx.call("bgnn_linear", ptr(ext), ptr(lay.p("lin_self")), n_own, fin, fout,
                              None, 0, 0.0, ptr(self.st[li]))
-            part.send_recv(ext, self.send[li])
+            if not halo_ready:
+                part.send_recv(ext, self.send[li])
             e1 = mark()
             ctx.call("bgnn_aggregate", dg.h, 1, ptr(ext), fin, ptr(agg))
             e2 = mark()
-            if split:
+            if remote_out:
+                # the next layer's input: own rows here, halo rows in the peers
+                main.wait_stream(self.side)
+                pr = self.peer
+                ctx.call("bgnn_linear_add_remote", ptr(agg), ptr(lay.p("lin_neighbor")), n_own,
+                         fin, fout, ptr(self.st[li]), ptr(lay.p("bias")), act, 0.0, ptr(out),
+                         ptr(pr.row_ptr), ptr(pr.dst), ptr(pr.tables[li]), ptr(pr.peer_rows),
+                         part.world)
+                # every rank's stores land before anyone reads its halo rows
+                dist.all_reduce(self.flag, group=part.group)
+            elif split:
                 main.wait_stream(self.side)
                 ctx.call("bgnn_linear_add", ptr(agg), ptr(lay.p("lin_neighbor")), n_own, fin,
                          fout, ptr(self.st[li]), ptr(lay.p("bias")), act, 0.0, ptr(out))
@@ -587,6 +634,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-spmm", action="store_true")
     ap.add_argument("--no-small", action="store_true")
+    ap.add_argument("--no-peer-stores", action="store_true",
+                    help="N>1: exchange every layer's halo rows with the all-to-all instead")
     ap.add_argument("--profile", choices=["small", "full-agg"], default=None,
                     help="run one profiling case for ncu and exit")
     args = ap.parse_args()
@@ -640,7 +689,7 @@ def main():
         part = HaloPlan(ei[:e], ei[e:], n, rank, world)
         dg = part.device_graph(local)
         x = x_full[part.lo:part.hi].contiguous()
-        psage = PartitionedSage(layers, part, dg, x, ctx)
+        psage = PartitionedSage(layers, part, dg, x, ctx, peer_stores=not args.no_peer_stores)
         step = psage.forward
     else:
         from browsergnn_b200.graph import DeviceGraph
@@ -780,12 +829,16 @@ def main():
         }
         if part is not None:
             line["config"]["halo_rows_rank0"] = part.n_halo
+            line["config"]["halo_exchange"] = (
+                "layer 1: NCCL all-to-all; layers 2-3: peer stores from the previous layer's "
+                "epilogue + one barrier" if psage.peer is not None else "NCCL all-to-all")
         if spmm is not None:
             line["spmm_sweep"] = spmm
         if small is not None:
             line["workloads"] = small
         print(json.dumps(line), flush=True)
     if world > 1:
+        psage.close()
         dist.barrier()
         dist.destroy_process_group()
 

@@ -93,6 +93,13 @@ SIGNATURES = {
     "bgnn_linear": [_P, _P, _P, _U32, _U32, _U32, _P, _I, _D, _P],
     "bgnn_sage_linear": [_P, _P, _P, _P, _P, _U32, _U32, _U32, _P, _I, _D, _P],
     "bgnn_linear_add": [_P, _P, _P, _U32, _U32, _U32, _P, _P, _I, _D, _P],
+    "bgnn_linear_add_remote": [_P, _P, _P, _U32, _U32, _U32, _P, _P, _I, _D, _P, _P, _P, _P, _P,
+                               _U32],
+    "bgnn_shared_alloc": [_P, _U64, ctypes.POINTER(_P)],
+    "bgnn_shared_free": [_P, _P],
+    "bgnn_ipc_handle": [_P, _P, _P],
+    "bgnn_ipc_open": [_P, _P, ctypes.POINTER(_P)],
+    "bgnn_ipc_close": [_P, _P],
     "bgnn_l2_normalize_rows": [_P, _P, _U32, _U32],
     "bgnn_sum_pool": [_P, _P, _U32, _U32, _P, _U32, _P],
     "bgnn_pack_rows": [_P, _P, _U32, _P, _U32, _U32, _P],

@@ -200,6 +200,12 @@ int bgnn_run_linear(bgnn_ctx* ctx, const float* a, const float* w, const float* 
 int bgnn_run_linear_add(bgnn_ctx* ctx, const float* a, const float* w, uint32_t m, uint32_t k,
                         uint32_t n, const float* addend, const float* bias, int act,
                         double act_param, float* out);
+// the same, with the rows of a remote map also stored into peers' buffers
+int bgnn_run_linear_add_remote(bgnn_ctx* ctx, const float* a, const float* w, uint32_t m,
+                               uint32_t k, uint32_t n, const float* addend, const float* bias,
+                               int act, double act_param, float* out, const uint32_t* row_ptr,
+                               const uint64_t* dst, float* const* peers,
+                               const uint32_t* peer_rows, uint32_t num_peers);
 int bgnn_run_activation(bgnn_ctx* ctx, int act, double param, const float* x, uint64_t n,
                         float* out);
 int bgnn_run_add(bgnn_ctx* ctx, const float* a, const float* b, uint64_t n, float* out);

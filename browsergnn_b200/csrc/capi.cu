@@ -495,6 +495,21 @@ extern "C" int bgnn_linear_add(bgnn_ctx* ctx, const float* a, const float* w, ui
   return bgnn_run_linear_add(ctx, a, w, m, k, n, addend, bias, act, act_param, out);
 }
 
+extern "C" int bgnn_linear_add_remote(bgnn_ctx* ctx, const float* a, const float* w, uint32_t m,
+                                      uint32_t k, uint32_t n, const float* addend,
+                                      const float* bias, int act, double act_param, float* out,
+                                      const uint32_t* row_ptr, const uint64_t* dst,
+                                      float* const* peers, const uint32_t* peer_rows,
+                                      uint32_t num_peers) {
+  BGNN_TRY(ctx_ok(ctx));
+  BGNN_TRY(check_act(ctx, act));
+  BGNN_REQUIRE(ctx, (a && w) || (uint64_t)m * k * n == 0, "NULL operand");
+  BGNN_REQUIRE(ctx, out || (uint64_t)m * n == 0, "NULL out");
+  BGNN_REQUIRE(ctx, row_ptr && peers && peer_rows && (dst || m == 0), "NULL remote map");
+  return bgnn_run_linear_add_remote(ctx, a, w, m, k, n, addend, bias, act, act_param, out,
+                                    row_ptr, dst, peers, peer_rows, num_peers);
+}
+
 extern "C" int bgnn_l2_normalize_rows(bgnn_ctx* ctx, float* x, uint32_t m, uint32_t n) {
   BGNN_TRY(ctx_ok(ctx));
   BGNN_REQUIRE(ctx, x || (uint64_t)m * n == 0, "NULL x");

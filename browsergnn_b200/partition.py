@@ -126,11 +126,134 @@ class HaloPlan:
         part)."""
         return self.send_recv(ext, self.pack_send(ext, pack))
 
+    def remote_map(self):
+        """Where each owned row goes in the other ranks' [owned | halo]
+        buffers, for producers that store rows straight into their peers'
+        memory instead of an all-to-all.  Rank p's halo holds its rows from
+        rank r at n_own(p) + (rows p receives from ranks < r) + k for the k-th
+        row r sends it.  Returns (row_ptr [n_own+1] int64, dst [n_send] int64
+        packing peer << 32 | destination row, in row order, each row's
+        destinations by peer), and peer_rows[p] = rows of p's buffer."""
+        import torch.distributed as dist
+
+        torch = _torch()
+        dev = self.halo.device
+        info = torch.tensor([self.n_own, self.n_halo] + self.recv_splits, dtype=torch.int64,
+                            device=dev)
+        allinfo = [torch.empty_like(info) for _ in range(self.world)]
+        dist.all_gather(allinfo, info, group=self.group)
+        allinfo = [t.cpu().tolist() for t in allinfo]
+        rows_l, dst_l = [], []
+        send_rows = self.send_rows.to(torch.int64).cpu()
+        send_rows = torch.where(send_rows < 0, send_rows + (1 << 32), send_rows)
+        pos = 0
+        for p in range(self.world):
+            cnt = self.send_splits[p]
+            if cnt == 0:
+                continue
+            n_own_p = allinfo[p][0]
+            off = sum(allinfo[p][2:2 + self.rank])  # rows p receives from ranks before me
+            rows_l.append(send_rows[pos:pos + cnt])
+            dst_l.append((p << 32) + n_own_p + off + torch.arange(cnt, dtype=torch.int64))
+            pos += cnt
+        peer_rows = [allinfo[p][0] + allinfo[p][1] for p in range(self.world)]
+        if not rows_l:
+            return torch.zeros(self.n_own + 1, dtype=torch.int64), \
+                torch.zeros(0, dtype=torch.int64), peer_rows
+        rows = torch.cat(rows_l)
+        dst = torch.cat(dst_l)
+        order = torch.argsort(rows, stable=True)
+        counts = torch.bincount(rows, minlength=self.n_own)
+        row_ptr = torch.zeros(self.n_own + 1, dtype=torch.int64)
+        row_ptr[1:] = torch.cumsum(counts, 0)
+        return row_ptr, dst[order], peer_rows
+
     def device_graph(self, device: Optional[int] = None):
         from .graph import DeviceGraph
 
         return DeviceGraph(self.edge_index, self.num_edges, self.n_own + self.n_halo, self.n_own,
                            device=device)
+
+
+class SharedBuffer:
+    """A [rows, cols] f32 device buffer in its own allocation
+    (bgnn_shared_alloc), viewed as a torch tensor; other ranks of the node can
+    map it by its IPC handle."""
+
+    def __init__(self, ctx, rows: int, cols: int):
+        import ctypes
+
+        torch = _torch()
+        self.ctx = ctx
+        p = ctypes.c_void_p()
+        ctx.call("bgnn_shared_alloc", int(rows) * int(cols) * 4, ctypes.byref(p))
+        self.ptr = p.value
+        self.__cuda_array_interface__ = {"shape": (int(rows), int(cols)), "typestr": "<f4",
+                                         "data": (self.ptr, False), "version": 2}
+        self.tensor = torch.as_tensor(self, device=f"cuda:{ctx.device}")
+
+    def handle(self) -> bytes:
+        import ctypes
+
+        buf = (ctypes.c_uint8 * 64)()
+        self.ctx.call("bgnn_ipc_handle", self.ptr, buf)
+        return bytes(buf)
+
+    def free(self):
+        if self.ptr:
+            self.tensor = None
+            self.ctx.call("bgnn_shared_free", self.ptr)
+            self.ptr = None
+
+
+class PeerStores:
+    """Everything a rank needs to store its layer outputs straight into the
+    other ranks' halo rows (bgnn_linear_add_remote): the remote map of a
+    HaloPlan on the device, and for each shared buffer the table of the
+    peers' mapped addresses (its own entry is NULL)."""
+
+    def __init__(self, plan: "HaloPlan", ctx, buffers: List[SharedBuffer]):
+        import ctypes
+
+        import torch.distributed as dist
+
+        torch = _torch()
+        self.plan, self.ctx = plan, ctx
+        dev = f"cuda:{ctx.device}"
+        row_ptr, dst, peer_rows = plan.remote_map()
+        if dst.numel():
+            peers = dst >> 32
+            rows = dst & 0xFFFFFFFF
+            lim = torch.tensor(peer_rows, dtype=torch.int64)[peers]
+            if bool((peers == plan.rank).any()) or bool((peers >= plan.world).any()) or \
+                    bool((rows < 0).any()) or bool((rows >= lim).any()):
+                raise ValueError("remote map out of range")
+        self.row_ptr = _as_u32_bits(row_ptr).to(dev)
+        self.dst = dst.to(dev)
+        self.peer_rows = _as_u32_bits(torch.tensor(peer_rows, dtype=torch.int64)).to(dev)
+        handles = [b.handle() for b in buffers]
+        everyone = [None] * plan.world
+        dist.all_gather_object(everyone, handles, group=plan.group)
+        self.opened = []
+        self.tables = []
+        for j in range(len(buffers)):
+            ptrs = []
+            for p in range(plan.world):
+                if p == plan.rank:
+                    ptrs.append(0)
+                    continue
+                h = (ctypes.c_uint8 * 64).from_buffer_copy(everyone[p][j])
+                q = ctypes.c_void_p()
+                ctx.call("bgnn_ipc_open", h, ctypes.byref(q))
+                self.opened.append(q.value)
+                ptrs.append(q.value)
+            self.tables.append(torch.tensor(ptrs, dtype=torch.int64, device=dev))
+
+    def close(self):
+        """Unmap the peers' buffers (before any rank frees its own)."""
+        for q in self.opened:
+            self.ctx.call("bgnn_ipc_close", q)
+        self.opened = []
 
 
 def _as_u32_bits(t):

@@ -265,6 +265,36 @@ BGNN_API int bgnn_sage_linear(bgnn_ctx* ctx, const float* agg, const float* x, c
 BGNN_API int bgnn_linear_add(bgnn_ctx* ctx, const float* a, const float* w, uint32_t m,
                              uint32_t k, uint32_t n, const float* addend, const float* bias,
                              int act, double act_param, float* out);
+/* ---- peer buffers for bgnn_linear_add_remote (one process per GPU) ----
+ * bgnn_shared_alloc: a device buffer of its own cudaMalloc allocation, so
+ * its IPC handle (bgnn_ipc_handle, BGNN_IPC_HANDLE_BYTES bytes) maps it
+ * from its first byte; another process of the node maps it with
+ * bgnn_ipc_open (peer access enabled on demand) and unmaps it with
+ * bgnn_ipc_close before the owner calls bgnn_shared_free. */
+#define BGNN_IPC_HANDLE_BYTES 64
+BGNN_API int bgnn_shared_alloc(bgnn_ctx* ctx, uint64_t bytes, void** out);
+BGNN_API int bgnn_shared_free(bgnn_ctx* ctx, void* p);
+BGNN_API int bgnn_ipc_handle(bgnn_ctx* ctx, void* base, uint8_t* handle_out);
+BGNN_API int bgnn_ipc_open(bgnn_ctx* ctx, const uint8_t* handle, void** out);
+BGNN_API int bgnn_ipc_close(bgnn_ctx* ctx, void* p);
+
+/* bgnn_linear_add for a row-partitioned graph on several GPUs of one node:
+ * each output row is also stored into the [owned | halo] buffers of the
+ * GPUs whose next layer reads it, so the next layer needs no all-to-all (the
+ * store happens in the epilogue that produces the row).  row_ptr [m+1] and
+ * dst (device arrays) list each row's destinations, dst packing
+ * peer << 32 | destination row; peers[p] (a device array) is rank p's buffer
+ * mapped into this process (CUDA IPC; plain stores, no multicast), rows of
+ * width n, peer_rows[p] rows long.  A destination out of range is reported as
+ * BGNN_ERR_OUT_OF_RANGE and skipped.  The caller orders the peers' reads
+ * after this kernel on every rank (e.g. a collective on the same streams).
+ * Fast math only; n % 4 == 0 and 16-byte aligned w, out and addend. */
+BGNN_API int bgnn_linear_add_remote(bgnn_ctx* ctx, const float* a, const float* w, uint32_t m,
+                                    uint32_t k, uint32_t n, const float* addend,
+                                    const float* bias, int act, double act_param, float* out,
+                                    const uint32_t* row_ptr, const uint64_t* dst,
+                                    float* const* peers, const uint32_t* peer_rows,
+                                    uint32_t num_peers);
 /* SAGE 'pool' aggregator projection (sage.ts:149-159) applied per node:
  * out[i,j] = f32(Math.max(0, bias[j] + sum_q x[i,q]*w[q,j])) with a double
  * accumulator; w is [k, k].  An edge's projected message depends only on its

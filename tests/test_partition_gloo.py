@@ -54,7 +54,23 @@ def _rank_main(rank, world, port, n, f, ei, e, x, want, q):
             got = orc.csr_aggregate(rp, so, plan.n_own, ext, f, op, threads=1).reshape(-1, f)
             res[op] = np.array_equal(got.view(np.uint32),
                                      want[op][plan.lo:plan.hi].view(np.uint32))
-        q.put((rank, ok_ext, res, plan.n_own, plan.n_halo, plan.num_edges))
+        # remote-store map: applying every rank's (peer, row) destinations to
+        # its owned rows must reproduce each rank's halo rows exactly
+        row_ptr, dst, peer_rows = plan.remote_map()
+        maps = [None] * world
+        dist.all_gather_object(maps, (plan.lo, plan.n_own, row_ptr.tolist(), dst.tolist(),
+                                      peer_rows))
+        buf = np.full((plan.n_own + plan.n_halo, f), np.nan, np.float32)
+        buf[: plan.n_own] = x[plan.lo:plan.hi]
+        ok_map = peer_rows[rank] == plan.n_own + plan.n_halo
+        for lo_p, n_own_p, rp_p, dst_p, _ in maps:
+            for i in range(n_own_p):
+                for d in dst_p[rp_p[i]:rp_p[i + 1]]:
+                    if (d >> 32) == rank:
+                        ok_map = ok_map and (d & 0xffffffff) >= plan.n_own
+                        buf[d & 0xffffffff] = x[lo_p + i]
+        ok_map = ok_map and np.array_equal(buf, x[need])
+        q.put((rank, ok_ext and ok_map, res, plan.n_own, plan.n_halo, plan.num_edges))
     finally:
         dist.destroy_process_group()
 
