@@ -201,7 +201,7 @@ class PartitionedSage:
     adds to it (bgnn_linear_add), the same two f32 results and the same final
     rounding as bgnn_sage_linear."""
 
-    def __init__(self, layers, part, dg, x, ctx, peer_stores=True):
+    def __init__(self, layers, part, dg, x, ctx, peer_stores=False):
         import torch
 
         from browsergnn_b200.partition import PeerStores, SharedBuffer
@@ -634,8 +634,10 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-spmm", action="store_true")
     ap.add_argument("--no-small", action="store_true")
-    ap.add_argument("--no-peer-stores", action="store_true",
-                    help="N>1: exchange every layer's halo rows with the all-to-all instead")
+    ap.add_argument("--peer-stores", action="store_true",
+                    help="N>1: layers 2-3 get their halo rows from the previous layer's epilogue "
+                         "storing into the peers' buffers instead of the all-to-all (bit-identical; "
+                         "faster at 2 GPUs, slower at 8: 16-byte peer stores use NVLink poorly)")
     ap.add_argument("--profile", choices=["small", "full-agg"], default=None,
                     help="run one profiling case for ncu and exit")
     args = ap.parse_args()
@@ -689,7 +691,7 @@ def main():
         part = HaloPlan(ei[:e], ei[e:], n, rank, world)
         dg = part.device_graph(local)
         x = x_full[part.lo:part.hi].contiguous()
-        psage = PartitionedSage(layers, part, dg, x, ctx, peer_stores=not args.no_peer_stores)
+        psage = PartitionedSage(layers, part, dg, x, ctx, peer_stores=args.peer_stores)
         step = psage.forward
     else:
         from browsergnn_b200.graph import DeviceGraph
