@@ -49,6 +49,7 @@ struct bgnn_graph {
   int has_self_loops = 0;
   bool csr_only = false;           // built from an existing CSR (no eid/out_deg)
   float* dinv[2] = {nullptr, nullptr};  // GCN D^-1/2 without / with loop tail
+  uint32_t* dst_of = nullptr;      // [E] destination row of each CSR slot (built on first use)
 };
 
 // ---------------------------------------------------------------------------
@@ -143,6 +144,7 @@ int bgnn_graph_from_csr(bgnn_ctx* ctx, const uint32_t* row_ptr, const uint32_t* 
                         uint32_t num_rows, uint32_t num_cols, bgnn_graph* g, bool copy);
 void bgnn_graph_free(bgnn_graph* g);
 int bgnn_graph_dinv(bgnn_ctx* ctx, bgnn_graph* g, int tail, const float** out);
+int bgnn_graph_dst_of(bgnn_ctx* ctx, bgnn_graph* g, const uint32_t** out);
 
 // ---------------------------------------------------------------------------
 // aggregation (aggregate.cu)

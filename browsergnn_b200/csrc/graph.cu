@@ -195,6 +195,7 @@ void bgnn_graph_free(bgnn_graph* g) {
   cudaFree(g->items);
   cudaFree(g->dinv[0]);
   cudaFree(g->dinv[1]);
+  cudaFree(g->dst_of);
   *g = bgnn_graph();
 }
 
@@ -300,6 +301,25 @@ int bgnn_graph_dinv(bgnn_ctx* ctx, bgnn_graph* g, int tail, const float** out) {
     BGNN_LAUNCHED(ctx);
   }
   *out = d;
+  return BGNN_OK;
+}
+
+// warp per row: every slot of the row gets the row's id
+__global__ void k_dst_of(const uint32_t* __restrict__ rp, uint32_t n, uint32_t* __restrict__ out) {
+  const uint32_t lane = threadIdx.x & 31;
+  for (uint32_t r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < n;
+       r += (gridDim.x * blockDim.x) >> 5)
+    for (uint32_t s = rp[r] + lane; s < rp[r + 1]; s += 32) out[s] = r;
+}
+
+int bgnn_graph_dst_of(bgnn_ctx* ctx, bgnn_graph* g, const uint32_t** out) {
+  if (!g->dst_of) {
+    BGNN_CUDA(ctx, cudaMalloc(&g->dst_of, (g->num_edges ? g->num_edges : 1) * 4));
+    k_dst_of<<<grid_for(ctx, (uint64_t)g->n_dst * 32, 256), 256, 0, ctx->stream>>>(
+        g->row_ptr, g->n_dst, g->dst_of);
+    BGNN_LAUNCHED(ctx);
+  }
+  *out = g->dst_of;
   return BGNN_OK;
 }
 
