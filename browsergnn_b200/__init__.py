@@ -31,6 +31,7 @@ from .nn import (GELU, Dropout, Linear, LogSoftmax, PReLU, SiLU, Sigmoid, Softma
                  manual_seed)
 from .models import ConceptPrerequisiteMapper, LearningPathRecommender, StudentMasteryPredictor
 from . import serialization
+from .graphs import CapturedForward
 from .serialization import (deserializeModel, getModelSize, getStateDict, loadModelFromJSON,
                             loadStateDict, saveModelToJSON, serializeModel)
 
@@ -45,4 +46,5 @@ __all__ = [
     "manual_seed", "StudentMasteryPredictor", "LearningPathRecommender",
     "ConceptPrerequisiteMapper", "serialization", "serializeModel", "deserializeModel",
     "saveModelToJSON", "loadModelFromJSON", "getStateDict", "loadStateDict", "getModelSize",
+    "CapturedForward",
 ]

@@ -106,6 +106,7 @@ SIGNATURES = {
     "bgnn_pool_projection": [_P, _P, _P, _P, _U32, _U32, _P],
     "bgnn_synth_rmat": [_P, _U64, _I, _U32, _U64, _D, _D, _D, _I, _P],
     "bgnn_dense": [_P, _P, _P, _U32, _U32, _U32, _P, _I, _D, _P],
+    "bgnn_segment_sum": [_P, _P, _U32, _P, _U32, _P],
     "bgnn_softmax_rows": [_P, _P, _U32, _U32, _P, _F, _I, _P],
     "bgnn_dropout": [_P, _P, _U64, _D, _U64, _P],
     "bgnn_prelu": [_P, _P, _U64, _P, _U32, _P],

@@ -290,6 +290,31 @@ int run_dense(bgnn_ctx* ctx, const float* x, const float* w, uint32_t m, uint32_
 
 }  // namespace
 
+// g[b, f] = sum of x[i, f] over the rows i of segment b, rows in order (one
+// CTA per segment, a thread per feature; the same f32 adds in the same order
+// as the scatter-add over a sorted batch vector)
+__global__ void k_segment_sum(const float* __restrict__ x, uint32_t f,
+                              const uint32_t* __restrict__ seg, float* __restrict__ out) {
+  const uint32_t b = blockIdx.x;
+  const uint32_t r0 = seg[b], r1 = seg[b + 1];
+  for (uint32_t c = threadIdx.x; c < f; c += blockDim.x) {
+    float acc = 0.0f;
+    for (uint32_t r = r0; r < r1; r++) acc = __fadd_rn(acc, x[(uint64_t)r * f + c]);
+    out[(uint64_t)b * f + c] = acc;
+  }
+}
+
+extern "C" int bgnn_segment_sum(bgnn_ctx* ctx, const float* x, uint32_t f,
+                                const uint32_t* seg_ptr, uint32_t num_graphs, float* out) {
+  BGNN_TRY(check_ctx(ctx));
+  if ((uint64_t)num_graphs * f == 0) return BGNN_OK;
+  BGNN_REQUIRE(ctx, x && seg_ptr && out, "NULL argument");
+  const unsigned threads = f >= 256 ? 256u : ((f + 31) / 32) * 32;
+  k_segment_sum<<<num_graphs, threads, 0, ctx->stream>>>(x, f, seg_ptr, out);
+  BGNN_LAUNCHED(ctx);
+  return BGNN_OK;
+}
+
 extern "C" int bgnn_dense(bgnn_ctx* ctx, const float* x, const float* w, uint32_t m, uint32_t k,
                           uint32_t n, const float* bias, int act, double act_param, float* out) {
   BGNN_TRY(check_ctx(ctx));

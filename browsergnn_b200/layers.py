@@ -358,8 +358,15 @@ class GINConv(Module):
             self.registerParameter("mlp_bias2", _param((self.outChannels,), zeros=True))
 
     def _eps(self) -> float:
+        # read back once per parameter tensor (a host read inside a forward
+        # would also stall the stream and break CUDA-graph capture)
         t = self.p("epsilon") if self.trainEpsilon else self._buffers["epsilon"]
-        return float(np.float32(t.detach().cpu().numpy().reshape(-1)[0]))
+        cached = getattr(self, "_eps_cache", None)
+        if cached is not None and cached[0] is t:
+            return cached[1]
+        v = float(np.float32(t.detach().cpu().numpy().reshape(-1)[0]))
+        self._eps_cache = (t, v)
+        return v
 
     def forward(self, input: GraphData, _act=None) -> GraphData:
         torch = _torch()
@@ -471,7 +478,32 @@ def global_sum_pool(graph: GraphData, num_graphs: Optional[int] = None):
     else:
         bnp = np.asarray(graph.batch, np.uint32)
         b = int(num_graphs if num_graphs is not None else (int(bnp.max()) + 1 if bnp.size else 0))
-        batch = torch.from_numpy(bnp.view(np.int32)).to(x.device)
+        batch, seg = _batch_device(graph, x.device, b)
+        if seg is not None:  # graphs' nodes contiguous (batchGraphs): segmented sums
+            out = torch.empty((b, graph.numFeatures), dtype=torch.float32, device=x.device)
+            ctx.call("bgnn_segment_sum", ptr(x), graph.numFeatures, ptr(seg), b, ptr(out))
+            return out
     out = torch.empty((b, graph.numFeatures), dtype=torch.float32, device=x.device)
     ctx.call("bgnn_sum_pool", ptr(x), graph.numNodes, graph.numFeatures, ptr(batch), b, ptr(out))
     return out
+
+
+def _batch_device(graph: GraphData, device, num_graphs: int):
+    """(batch vector, segment offsets or None) on the device, built once and
+    kept with the graph's device structure (shared by every withFeatures
+    copy).  Offsets exist when the batch vector is non-decreasing and within
+    num_graphs, i.e. every graph's nodes are contiguous."""
+    torch = _torch()
+    dg = graph.device_graph(device.index)
+    key = (str(device), int(num_graphs))
+    cached = getattr(dg, "_batch_dev", None)
+    if cached is not None and cached[0] == key:
+        return cached[1], cached[2]
+    bnp = np.asarray(graph.batch, np.uint32)
+    t = torch.from_numpy(bnp.view(np.int32)).to(device)
+    seg = None
+    if bnp.size == 0 or (np.all(bnp[1:] >= bnp[:-1]) and int(bnp[-1]) < num_graphs):
+        offs = np.searchsorted(bnp, np.arange(num_graphs + 1), side="left").astype(np.uint32)
+        seg = torch.from_numpy(offs.view(np.int32)).to(device)
+    dg._batch_dev = (key, t, seg)
+    return t, seg

@@ -306,6 +306,13 @@ BGNN_API int bgnn_l2_normalize_rows(bgnn_ctx* ctx, float* x, uint32_t m, uint32_
 /* Global sum pool: g[b,:] = sum over nodes i with batch[i] == b, node order. */
 BGNN_API int bgnn_sum_pool(bgnn_ctx* ctx, const float* x, uint32_t num_nodes, uint32_t num_features,
                   const uint32_t* batch, uint32_t num_graphs, float* out);
+/* The same pool when every graph's nodes are contiguous (batchGraphs lays
+ * them out so, graph.ts:439-492): graph b owns rows seg_ptr[b] ..
+ * seg_ptr[b+1]-1 (device array, num_graphs+1 entries, non-decreasing,
+ * seg_ptr[num_graphs] <= num rows of x).  No temporary structures, so it can
+ * be captured in a CUDA graph. */
+BGNN_API int bgnn_segment_sum(bgnn_ctx* ctx, const float* x, uint32_t num_features,
+                              const uint32_t* seg_ptr, uint32_t num_graphs, float* out);
 
 /* ---- partitioning support (node-partitioned multi-GPU) ------------------ */
 /* out[i,:] = x[rows[i],:]  (halo pack; same kernel as gather) */

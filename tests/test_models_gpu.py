@@ -373,3 +373,35 @@ def test_pinned_host_graphdata_overlaps_upload(bg):
     got = conv.forward(g).x.cpu().numpy()
     assert_bits_equal(got, want, "pinned-host GraphData")
     assert g.addSelfLoops().numEdges >= e
+
+
+def test_captured_forward_replays_bits(bg):
+    """A GIN stack + pool captured in a CUDA graph replays the eager bits, and
+    picks up new features written into the captured input buffer."""
+    import torch
+
+    rng = np.random.default_rng(21)
+    n, f = 2000, 32
+    ei, e = rand_graph(n, 12000, 9, hub_deg=400)
+    x = rng.standard_normal((n, f)).astype(np.float32)
+    batch = np.sort(rng.integers(0, 40, n)).astype(np.uint32)
+    g = bg.GraphData(x=x, numNodes=n, numFeatures=f, edgeIndex=ei, numEdges=e, batch=batch)
+    gd = g.withFeatures(g.x_device())
+    layers = [bg.GINConv(inChannels=f, outChannels=64), bg.GINConv(inChannels=64, outChannels=64)]
+    for lay in layers:
+        _inject(bg, lay, rng, scale=0.2)
+
+    def step():
+        h = gd
+        for i, lay in enumerate(layers):
+            h = lay.forward(h, _act="relu" if i == 0 else None)
+        return bg.global_sum_pool(h, 40)
+
+    eager = step().cpu().numpy()
+    cap = bg.CapturedForward(step)
+    assert_bits_equal(cap().cpu().numpy(), eager, "replay")
+    x2 = rng.standard_normal((n, f)).astype(np.float32)
+    gd.x.copy_(torch.from_numpy(x2).cuda())
+    want2 = step().cpu().numpy()
+    assert_bits_equal(cap().cpu().numpy(), want2, "replay with new features")
+    cap.close()
