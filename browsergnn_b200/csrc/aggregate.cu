@@ -54,9 +54,12 @@ __device__ __forceinline__ float init_acc() {
   return OP == OP_MAX ? -INFINITY : 0.0f;
 }
 
+// rinv: 1/cnt already computed (the streaming pipes compute it once per row
+// into shared memory rather than in every warp of the row)
 __device__ __forceinline__ float epilogue(float v, const AggArgs& a, uint32_t row, int f,
-                                          uint32_t cnt) {
-  if (a.mean && cnt > 0) v = __double2float_rn(__dmul_rn((double)v, __ddiv_rn(1.0, (double)cnt)));
+                                          uint32_t cnt, const double* rinv = nullptr) {
+  if (a.mean && cnt > 0)
+    v = __double2float_rn(__dmul_rn((double)v, rinv ? *rinv : __ddiv_rn(1.0, (double)cnt)));
   if (a.max_fix && v == -INFINITY) v = 0.0f;
   if (a.gin_x) {
     // GINConv: combined = (1 + eps) * x + aggregated, in double (gin.ts:150-157)
@@ -321,7 +324,7 @@ template <int OP, int CP, int S = ST_S, bool ONE_ROW = false>
 __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint32_t re, int f0,
                                              int fw, int swp, int tp, int ptid, int eps,
                                              float* buf, float* wbuf, uint32_t* sidx, uint32_t* rps,
-                                             float* rdv, uint32_t& kg,
+                                             float* rdv, double* rinv, uint32_t& kg,
                                              int bar_id) {
   const uint32_t e0 = a.row_ptr[rb];
   const uint32_t ne = a.row_ptr[re] - e0;
@@ -329,6 +332,9 @@ __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint
   for (uint32_t i = ptid; i <= nrows; i += tp) rps[i] = a.row_ptr[rb + i] - e0;
   if (OP == OP_GCN)
     for (uint32_t i = ptid; i < nrows; i += tp) rdv[i] = a.dinv[rb + i];
+  if (rinv != nullptr)  // mean: 1/count in double, one division per row
+    for (uint32_t i = ptid; i < nrows; i += tp)
+      rinv[i] = __ddiv_rn(1.0, (double)(a.row_ptr[rb + i + 1] - a.row_ptr[rb + i]));
 
   const uint32_t nst = (ne + eps - 1) / eps;
   // Source ids: sidx slot m % (S+1) holds stage m's ids.  Stages 0..S-2 are
@@ -401,15 +407,22 @@ __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint
   pipe_bar(bar_id, tp);
 #pragma unroll
   for (int k = 0; k < S - 1; k++) issue((uint32_t)k);
+  // Consumers: thread ptid reduces feature f0 + ptid, one serial chain in
+  // edge order.  (Four features per thread, with one 16-byte shared load per
+  // edge and a quarter of the warps paying the per-edge bookkeeping, measured
+  // slower: 21.0 vs 11.0 ms at F = 256.  A consumer warp then stalls on each
+  // load with no other consumer warp on its scheduler to cover it.)
   const bool consumer = ptid < fw;
+  const int fv = f0 + ptid;
   float acc = init_acc<OP>();
   uint32_t r = 0;
   uint32_t nxt = rps[1];
   float dinv_r = (OP == OP_GCN && nrows) ? rdv[0] : 0.0f;
   auto finalize = [&]() {
     const uint32_t row = rb + r;
-    const int f = f0 + ptid;
-    a.out[(int64_t)row * a.ld_out + f] = epilogue(acc, a, row, f, rps[r + 1] - rps[r]);
+    const uint32_t cnt_r = rps[r + 1] - rps[r];
+    const double* ri = rinv ? rinv + r : nullptr;
+    a.out[(int64_t)row * a.ld_out + fv] = epilogue(acc, a, row, fv, cnt_r, ri);
     acc = init_acc<OP>();
     r++;
     if (r < nrows) {
@@ -417,6 +430,7 @@ __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint
       if (OP == OP_GCN) dinv_r = rdv[r];
     }
   };
+  constexpr bool HAS_W = OP == OP_GCN || OP == OP_SPMM || OP == OP_SPMM_X;
   for (uint32_t k = 0; k < nst; k++) {
     const int slot = (int)((kg + k) % S);
     cp_async_wait<S - 2>();  // this thread's copies of stage k have landed
@@ -430,7 +444,6 @@ __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint
       const float* wb = wbuf + slot * eps;
       const uint32_t cnt = min((uint32_t)eps, ne - k * (uint32_t)eps);
       constexpr int R = 16;
-      constexpr bool HAS_W = OP == OP_GCN || OP == OP_SPMM || OP == OP_SPMM_X;
       float v[R], wr[R];
 #pragma unroll
       for (int u = 0; u < R; u++) {
@@ -473,7 +486,7 @@ __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint
 #pragma unroll
         for (int u = 0; u < UB; u++) {
           v[u] = b[(size_t)(j + u) * swp];
-          wr[u] = (OP == OP_GCN || OP == OP_SPMM || OP == OP_SPMM_X) ? wb[j + u] : 0.0f;
+          wr[u] = HAS_W ? wb[j + u] : 0.0f;
         }
         if (nxt >= base + j + UB) {  // no row ends inside this block
 #pragma unroll
@@ -509,7 +522,7 @@ __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint
 template <int OP, bool A16>
 __global__ void __launch_bounds__(ST_THREADS, 2)
     k_agg_stream(const AggArgs a, int P, int swp, int n_slices, uint32_t n_giant, int gsw,
-                 int eps_g, int mode, uint32_t n_ex, uint32_t* queue) {
+                 int eps_g, int mode, uint32_t n_ex, uint32_t* queue, int mean_rinv) {
   extern __shared__ float4 st_smem4[];
   float* data = reinterpret_cast<float*>(st_smem4);
   const size_t data_f = stream_data_floats(P, swp);
@@ -520,6 +533,10 @@ __global__ void __launch_bounds__(ST_THREADS, 2)
   uint32_t* rps = sidx + stream_sidx_words(P);
   int* slots = reinterpret_cast<int*>(rps + P * (ST_RMAX + 1));  // [0..P] fetched items
   float* rdv = reinterpret_cast<float*>(slots + 16);  // present for OP_GCN only
+  // present for a mean with P <= 2 only: 8-byte aligned after slots
+  double* rinv = mean_rinv ? reinterpret_cast<double*>(
+                                 (reinterpret_cast<uintptr_t>(slots + 16) + 7) & ~uintptr_t(7))
+                           : nullptr;
   const int F = a.num_features;
   const uint32_t gs = (uint32_t)((F + gsw - 1) / gsw);
   const uint32_t giant_work = n_giant * gs;
@@ -527,6 +544,11 @@ __global__ void __launch_bounds__(ST_THREADS, 2)
   const uint32_t light_work = (a.n_items - a.n_heavy_items) * (uint32_t)n_slices;
   const int tp = ST_THREADS / P;
   constexpr int CP = A16 ? CP_A16 : CP_A4;  // rows 16-byte aligned: 16-byte copies
+  auto run = [&](uint32_t rb, uint32_t re, int f0, int fw, int width, int tpp, int pt, int eps,
+                 float* d, float* w_, uint32_t* si, uint32_t* rp, float* dv, double* ri,
+                 uint32_t& kgr, int bar) {
+    stream_range<OP, CP>(a, rb, re, f0, fw, width, tpp, pt, eps, d, w_, si, rp, dv, ri, kgr, bar);
+  };
 
   // Giant rows (the first n_giant heavy items, chosen at launch) are cut into
   // gsw-feature slices with eps_g edges per stage, so several CTAs stream one
@@ -544,14 +566,14 @@ __global__ void __launch_bounds__(ST_THREADS, 2)
     if (w < giant_work) {
       const uint2 item = a.items[w / gs];
       const int f0 = (int)(w % gs) * gsw;
-      stream_range<OP, CP>(a, item.x, item.y, f0, min(gsw, F - f0), gsw, ST_THREADS,
-                                threadIdx.x, eps_g, data, wb, sidx, rps, rdv, kg, 0);
+      run(item.x, item.y, f0, min(gsw, F - f0), gsw, ST_THREADS, threadIdx.x, eps_g, data, wb, sidx,
+          rps, rdv, rinv, kg, 0);
     } else {
       const uint32_t w2 = w - giant_work;
       const uint2 item = a.items[n_giant + w2 / (uint32_t)n_slices];
       const int f0 = (int)(w2 % (uint32_t)n_slices) * ST_SW;
-      stream_range<OP, CP>(a, item.x, item.y, f0, min(ST_SW, F - f0), swp, ST_THREADS,
-                           threadIdx.x, ST_EPS * P, data, wb, sidx, rps, rdv, kg, 0);
+      run(item.x, item.y, f0, min(ST_SW, F - f0), swp, ST_THREADS, threadIdx.x, ST_EPS * P, data, wb,
+          sidx, rps, rdv, rinv, kg, 0);
     }
   }
   // phase 2: light items, P independent pipes
@@ -562,6 +584,7 @@ __global__ void __launch_bounds__(ST_THREADS, 2)
   uint32_t* psidx = sidx + pipe * (ST_S + 1) * ST_EPS;
   uint32_t* prps = rps + pipe * (ST_RMAX + 1);
   float* prdv = rdv + pipe * ST_RMAX;
+  double* prinv = rinv ? rinv + pipe * ST_RMAX : nullptr;
   uint32_t kgp = 0;
   for (;;) {
     if (ptid == 0) slots[pipe] = (int)atomicAdd(&queue[1], 1u);
@@ -570,8 +593,8 @@ __global__ void __launch_bounds__(ST_THREADS, 2)
     if (w >= light_work) break;
     const uint2 item = a.items[a.n_heavy_items + w / (uint32_t)n_slices];
     const int f0 = (int)(w % (uint32_t)n_slices) * ST_SW;
-    stream_range<OP, CP>(a, item.x, item.y, f0, min(ST_SW, F - f0), swp, tp, ptid, ST_EPS, pdata,
-                         pwb, psidx, prps, prdv, kgp, bar_id);
+    run(item.x, item.y, f0, min(ST_SW, F - f0), swp, tp, ptid, ST_EPS, pdata, pwb, psidx, prps, prdv,
+        prinv, kgp, bar_id);
   }
 }
 
@@ -601,7 +624,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
     const uint2 item = a.items[w / gs];
     const int f0 = (int)(w % gs) * gsw;
     stream_range<OP, CP, GS_S, true>(a, item.x, item.y, f0, min(gsw, F - f0), gsw, ST_THREADS,
-                                     threadIdx.x, eps_g, data, wb, sidx, rps, rdv, kg, 0);
+                                     threadIdx.x, eps_g, data, wb, sidx, rps, rdv, nullptr, kg, 0);
   }
 }
 
@@ -610,6 +633,8 @@ int launch_stream_t(bgnn_ctx* ctx, const AggArgs& a, int P, int swp, int n_slice
   size_t smem = (stream_data_floats(P, swp) + stream_w_floats(P) + stream_sidx_words(P) +
                  (size_t)P * (ST_RMAX + 1) + 16) * 4;
   if (OP == OP_GCN) smem += (size_t)P * ST_RMAX * 4;
+  const int mean_rinv = (OP == OP_SUM && a.mean && P <= 2) ? 1 : 0;
+  if (mean_rinv) smem += (size_t)P * ST_RMAX * 8 + 8;
   BGNN_CUDA(ctx, cudaFuncSetAttribute(k_agg_stream<OP, A16>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   int per_sm = 0;
@@ -670,7 +695,7 @@ int launch_stream_t(bgnn_ctx* ctx, const AggArgs& a, int P, int swp, int n_slice
     mode = 2;
   }
   k_agg_stream<OP, A16><<<(unsigned)grid, ST_THREADS, smem, ctx->stream>>>(
-      a, P, swp, n_slices, n_giant, gsw, eps_g, mode, n_ex, queue);
+      a, P, swp, n_slices, n_giant, gsw, eps_g, mode, n_ex, queue, mean_rinv);
   BGNN_LAUNCHED(ctx);
   if (n_ex > 0) BGNN_CUDA(ctx, cudaStreamWaitEvent(ctx->stream, ctx->ev_join, 0));
   return BGNN_OK;
