@@ -540,8 +540,14 @@ __global__ void __launch_bounds__(ST_THREADS, 2)
   const int F = a.num_features;
   const uint32_t gs = (uint32_t)((F + gsw - 1) / gsw);
   const uint32_t giant_work = n_giant * gs;
-  const uint32_t heavy_work = giant_work + (a.n_heavy_items - n_giant) * (uint32_t)n_slices;
-  const uint32_t light_work = (a.n_items - a.n_heavy_items) * (uint32_t)n_slices;
+  // With several pipes per CTA (slices of at most 128 features), a heavy row
+  // streamed by the whole CTA would have no more consumer threads than one
+  // pipe (one per feature either way) and would restart the ring for a few
+  // stages: the pipes take those rows instead, at the front of their queue
+  // (largest first).  Phase 1 then runs only the giant-row slices.
+  const uint32_t first_light = P > 1 ? n_giant : a.n_heavy_items;
+  const uint32_t heavy_work = giant_work + (first_light - n_giant) * (uint32_t)n_slices;
+  const uint32_t light_work = (a.n_items - first_light) * (uint32_t)n_slices;
   const int tp = ST_THREADS / P;
   constexpr int CP = A16 ? CP_A16 : CP_A4;  // rows 16-byte aligned: 16-byte copies
   auto run = [&](uint32_t rb, uint32_t re, int f0, int fw, int width, int tpp, int pt, int eps,
@@ -576,7 +582,7 @@ __global__ void __launch_bounds__(ST_THREADS, 2)
           sidx, rps, rdv, rinv, kg, 0);
     }
   }
-  // phase 2: light items, P independent pipes
+  // phase 2: light items (with P > 1 also the non-giant heavy rows), P pipes
   const int pipe = threadIdx.x / tp, ptid = threadIdx.x % tp;
   const int bar_id = P == 1 ? 0 : pipe + 1;
   float* pdata = data + (size_t)pipe * ST_S * ST_EPS * swp;
@@ -591,7 +597,7 @@ __global__ void __launch_bounds__(ST_THREADS, 2)
     pipe_bar(bar_id, tp);
     const uint32_t w = (uint32_t)slots[pipe];
     if (w >= light_work) break;
-    const uint2 item = a.items[a.n_heavy_items + w / (uint32_t)n_slices];
+    const uint2 item = a.items[first_light + w / (uint32_t)n_slices];
     const int f0 = (int)(w % (uint32_t)n_slices) * ST_SW;
     run(item.x, item.y, f0, min(ST_SW, F - f0), swp, tp, ptid, ST_EPS, pdata, pwb, psidx, prps, prdv,
         prinv, kgp, bar_id);
