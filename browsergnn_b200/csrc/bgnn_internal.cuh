@@ -145,6 +145,7 @@ int bgnn_graph_from_csr(bgnn_ctx* ctx, const uint32_t* row_ptr, const uint32_t* 
 void bgnn_graph_free(bgnn_graph* g);
 int bgnn_graph_dinv(bgnn_ctx* ctx, bgnn_graph* g, int tail, const float** out);
 int bgnn_graph_dst_of(bgnn_ctx* ctx, bgnn_graph* g, const uint32_t** out);
+int bgnn_graph_dst_of_into(bgnn_ctx* ctx, const bgnn_graph* g, uint32_t* out);
 
 // ---------------------------------------------------------------------------
 // aggregation (aggregate.cu)

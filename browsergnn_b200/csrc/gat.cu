@@ -365,10 +365,13 @@ __global__ void __launch_bounds__(GH_THREADS) k_gat_heavy(const GatArgs a) {
   }
 }
 
+// dst_given: a slot -> destination row map the caller already built (the
+// allocation-free entry point); otherwise the graph's own, built on first use
 template <int KO>
-int launch_gat(bgnn_ctx* ctx, const GatArgs& a) {
-  const uint32_t* dst_of = nullptr;
-  BGNN_TRY(bgnn_graph_dst_of(ctx, const_cast<bgnn_graph*>(a.graph), &dst_of));
+int launch_gat(bgnn_ctx* ctx, const GatArgs& a, const uint32_t* dst_given = nullptr) {
+  const uint32_t* dst_of = dst_given;
+  if (dst_of == nullptr)
+    BGNN_TRY(bgnn_graph_dst_of(ctx, const_cast<bgnn_graph*>(a.graph), &dst_of));
   const uint64_t items = (a.num_edges + (a.tail ? a.n_rows : 0u)) * (uint64_t)a.heads;
   uint64_t ab = (items + 255) / 256;
   if (ab > (uint64_t)ctx->num_sms * 32) ab = (uint64_t)ctx->num_sms * 32;
@@ -456,11 +459,14 @@ int bgnn_run_gat(bgnn_ctx* ctx, const bgnn_graph* g, const float* h, uint32_t he
 // embedded in a JavaScript runtime, for instance) whose device memory is
 // owned by someone else.  The caller still provides every input and output.
 //
-// The array holds BGNN_GAT_NOALLOC_MAX_FLOATS floats (16 MiB); every GPU that
-// loads this library keeps it until the process exits.  A call needs
-// (edges + appended self-loops) * heads floats.  All calls share the one
-// array, so calls whose kernels overlap on the GPU race on it; the kernel
-// writes each slot before reading it, so nothing needs clearing between calls.
+// The array holds BGNN_GAT_NOALLOC_MAX_FLOATS 4-byte words (16 MiB); every
+// GPU that loads this library keeps it until the process exits.  A call
+// needs (edges + appended self-loops) * heads words for the attention values
+// plus one word per edge for the slot -> destination map (rebuilt in the array
+// on every call, so the graph's own lazily allocated map is never touched).
+// All calls share the one array, so calls whose kernels overlap on the GPU
+// race on it; every word a call reads it has written first, so nothing needs
+// clearing between calls.
 // ---------------------------------------------------------------------------
 #define BGNN_GAT_NOALLOC_MAX_FLOATS (4u << 20)
 
@@ -509,15 +515,19 @@ extern "C" int bgnn_gat_noalloc(bgnn_ctx* ctx, const bgnn_graph* g, const float*
     return bgnn_set_error(ctx, BGNN_ERR_UNSUPPORTED, "GAT output width %u exceeds 256", od);
   BGNN_REQUIRE(ctx, g->n_src == g->n_dst, "GAT needs a square graph");
   const int tail = (add_self_loops && !g->has_self_loops) ? 1 : 0;  // gat.ts:116-118
-  const uint64_t need = (g->num_edges + (tail ? g->n_dst : 0)) * (uint64_t)heads;
+  const uint64_t n_alpha = (g->num_edges + (tail ? g->n_dst : 0)) * (uint64_t)heads;
+  const uint64_t need = n_alpha + g->num_edges;
   if (need > BGNN_GAT_NOALLOC_MAX_FLOATS)
     return bgnn_set_error(ctx, BGNN_ERR_INVALID_ARG,
-                          "allocation-free GAT needs %llu scratch floats; the limit is %u "
-                          "((edges + self-loops) * heads)",
+                          "allocation-free GAT needs %llu scratch words; the limit is %u "
+                          "((edges + self-loops) * heads + edges)",
                           (unsigned long long)need, BGNN_GAT_NOALLOC_MAX_FLOATS);
   if (g->n_dst == 0) return BGNN_OK;
   float* scratch = nullptr;
   BGNN_TRY(noalloc_scratch(ctx, &scratch));
+  // the slot -> destination map goes after the attention values
+  uint32_t* dst_of = reinterpret_cast<uint32_t*>(scratch + n_alpha);
+  BGNN_TRY(bgnn_graph_dst_of_into(ctx, g, dst_of));
   GatArgs a;
   a.row_ptr = g->row_ptr;
   a.src_of = g->src_of;
@@ -547,8 +557,8 @@ extern "C" int bgnn_gat_noalloc(bgnn_ctx* ctx, const bgnn_graph* g, const float*
   a.n_heavy = g->heavy_rows ? g->n_heavy : 0u;
   a.heavy_threshold = g->heavy_threshold;
   const int ko = (int)((od + 31) / 32);
-  if (ko <= 1) return launch_gat<1>(ctx, a);
-  if (ko <= 2) return launch_gat<2>(ctx, a);
-  if (ko <= 4) return launch_gat<4>(ctx, a);
-  return launch_gat<8>(ctx, a);
+  if (ko <= 1) return launch_gat<1>(ctx, a, dst_of);
+  if (ko <= 2) return launch_gat<2>(ctx, a, dst_of);
+  if (ko <= 4) return launch_gat<4>(ctx, a, dst_of);
+  return launch_gat<8>(ctx, a, dst_of);
 }

@@ -312,6 +312,15 @@ __global__ void k_dst_of(const uint32_t* __restrict__ rp, uint32_t n, uint32_t* 
     for (uint32_t s = rp[r] + lane; s < rp[r + 1]; s += 32) out[s] = r;
 }
 
+// the same map written into a caller's buffer of num_edges words (no allocation)
+int bgnn_graph_dst_of_into(bgnn_ctx* ctx, const bgnn_graph* g, uint32_t* out) {
+  if (g->num_edges == 0) return BGNN_OK;
+  k_dst_of<<<grid_for(ctx, (uint64_t)g->n_dst * 32, 256), 256, 0, ctx->stream>>>(g->row_ptr,
+                                                                                 g->n_dst, out);
+  BGNN_LAUNCHED(ctx);
+  return BGNN_OK;
+}
+
 int bgnn_graph_dst_of(bgnn_ctx* ctx, bgnn_graph* g, const uint32_t** out) {
   if (!g->dst_of) {
     BGNN_CUDA(ctx, cudaMalloc(&g->dst_of, (g->num_edges ? g->num_edges : 1) * 4));

@@ -229,9 +229,10 @@ BGNN_API int bgnn_gat_train(bgnn_ctx* ctx, const bgnn_graph* g, const float* h, 
  * that reserves its memory budget at start-up, or a host application (such as
  * a Node-API addon inside a JavaScript runtime) whose device memory belongs to
  * someone else.  Same arguments and results as bgnn_gat; its per-edge
- * attention scratch lives in a fixed 16 MiB device array that every GPU
- * loading this library keeps until exit, so (edges + appended self-loops) *
- * heads must not exceed 4,194,304 (larger graphs get BGNN_ERR_INVALID_ARG).
+ * attention scratch and its slot -> row map live in a fixed 16 MiB device
+ * array that every GPU loading this library keeps until exit, so
+ * (edges + appended self-loops) * heads + edges must not exceed 4,194,304
+ * (larger graphs get BGNN_ERR_INVALID_ARG).
  * The first call on a device looks up the array's device address; make that
  * first call before any stream capture begins.  All calls share the array:
  * calls that overlap on the GPU race on it. */
