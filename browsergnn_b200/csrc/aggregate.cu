@@ -650,18 +650,23 @@ int launch_stream_t(bgnn_ctx* ctx, const AggArgs& a, int P, int swp, int n_slice
   const uint64_t work = (uint64_t)a.n_items * n_slices;
   uint64_t grid = (uint64_t)ctx->num_sms * per_sm;
   if (grid > work) grid = work ? work : 1;
-  // Giant rows: a heavy row whose bytes exceed one CTA's fair share of the
+  // Giant rows: a heavy row whose bytes exceed one pipe's fair share of the
   // launch would finish long after the rest, so it is cut into feature slices
-  // that separate CTAs stream.  The slice is the widest power of two from 128
+  // that separate CTAs stream (a single slice when F <= ST_GSW: the row then
+  // still gets a whole CTA and its larger stages).  The slice is the widest power of two from 128
   // down to ST_GSW features that keeps the largest row's slice within the
   // share (ST_GSW at least), with ST_GSTAGE floats per stage (eps_g edges x
   // gsw features).
   const int F = a.num_features;
   uint32_t n_giant = 0;
   int gsw = ST_GSW;
-  if (a.heavy_deg != nullptr && F > ST_GSW && grid > 1) {
+  if (a.heavy_deg != nullptr && grid > 1) {
+    // a heavy row otherwise runs in one pipe (1/P of a CTA): it is giant once
+    // its bytes exceed a pipe's share; its slices then get whole CTAs
     const double share = (double)a.num_edges * (double)F * 4.0 / (double)grid;
-    while (n_giant < a.n_heavy_items && (double)a.heavy_deg[n_giant] * F * 4.0 > share) n_giant++;
+    const double pipe_share = share / (double)P;
+    while (n_giant < a.n_heavy_items && (double)a.heavy_deg[n_giant] * F * 4.0 > pipe_share)
+      n_giant++;
     if (n_giant) {
       gsw = 128;
       while (gsw > ST_GSW && (gsw >= F || (double)a.heavy_deg[0] * gsw * 4.0 > share)) gsw >>= 1;
