@@ -78,14 +78,21 @@ struct RemoteRows {
   int* err = nullptr;
 };
 
-template <int BN, bool EXACT, bool B16, bool V4OUT, bool REMOTE = false>
+// DUAL (the SAGE pair in one launch): the tile first runs A*B over k and
+// stores it, rounded to f32, into its own outputs of C (the reference's
+// St tensor); it then runs A2*B2 over k with that stored St as the addend,
+// i.e. C = act(f32(f32(St + A2*B2) + bias)), bit for bit what two launches
+// give, with one tile start-up and one launch instead of two.
+template <int BN, bool EXACT, bool B16, bool V4OUT, bool REMOTE = false, bool DUAL = false>
 __global__ void __launch_bounds__(256, 2) k_sgemm_pipe(const float* __restrict__ A,
                                                        const float* __restrict__ B, uint32_t m,
                                                        uint32_t k, uint32_t n,
                                                        const float* addend,
                                                        const float* __restrict__ bias, int act,
                                                        double act_param, float* C,
-                                                       const RemoteRows rr) {
+                                                       const RemoteRows rr,
+                                                       const float* __restrict__ A2,
+                                                       const float* __restrict__ B2) {
   constexpr int TN = BN / 16;                 // 8 or 4 columns per thread
   constexpr int AST = PG_BM + PG_APAD;        // As row stride (floats)
   constexpr int A_STAGE = PG_BK * AST, B_STAGE = PG_BK * BN;
@@ -97,7 +104,8 @@ __global__ void __launch_bounds__(256, 2) k_sgemm_pipe(const float* __restrict__
   const int tx = tid & 15, ty = tid >> 4;
   const uint64_t m0 = (uint64_t)blockIdx.x * PG_BM;
   const uint32_t n0 = blockIdx.y * BN;
-  const uint32_t ntiles = (k + PG_BK - 1) / PG_BK;
+  const uint32_t nt1 = (k + PG_BK - 1) / PG_BK;  // k tiles per product
+  const uint32_t ntiles = DUAL ? 2 * nt1 : nt1;
 
   // Per-thread copy pattern, fixed for every tile.  A: the thread copies
   // columns a_kk and a_kk + 8 of rows a_r + 32 j (j < 4); a warp covers 4
@@ -115,21 +123,32 @@ __global__ void __launch_bounds__(256, 2) k_sgemm_pipe(const float* __restrict__
   const bool b_col_ok = n0 + b_c < n;
   const float* b_src = B + (uint64_t)b_kk * n + n0 + b_c;
   float* b_dst = Bs + b_kk * BN + b_c;
+  const float* a2_src = DUAL ? A2 + (m0 + a_r) * k + a_kk : nullptr;
+  const float* b2_src = DUAL ? B2 + (uint64_t)b_kk * n + n0 + b_c : nullptr;
 
   auto load_stage = [&](uint32_t t, int slot) {
+    const float* as_ = a_src;
+    const float* bs_ = b_src;
+    if constexpr (DUAL) {
+      if (t >= nt1) {  // the second product
+        t -= nt1;
+        as_ = a2_src;
+        bs_ = b2_src;
+      }
+    }
     const uint32_t k0 = t * PG_BK;
 #pragma unroll
     for (int i = 0; i < (PG_BM * PG_BK) / 256; i++) {
       const int dk = 8 * (i % (PG_BK / 8)), dr = 32 * (i / (PG_BK / 8));
       const bool ok = k0 + a_kk + dk < k && m0 + a_r + dr < m;
       cpa4_zfill(a_dst + slot * A_STAGE + dk * AST + dr,
-                 ok ? a_src + (uint64_t)dr * k + k0 + dk : A, ok);
+                 ok ? as_ + (uint64_t)dr * k + k0 + dk : A, ok);
     }
 #pragma unroll
     for (int i = 0; i < B_PASSES; i++) {
       const uint32_t gk = k0 + b_kk + B_ROWS * i;
       const bool ok = b_col_ok && gk < k;
-      const float* src = ok ? b_src + (uint64_t)(k0 + B_ROWS * i) * n : B;
+      const float* src = ok ? bs_ + (uint64_t)(k0 + B_ROWS * i) * n : B;
       float* dst = b_dst + slot * B_STAGE + B_ROWS * i * BN;
       if constexpr (B16)
         cpa16_zfill(dst, src, ok);
@@ -200,7 +219,8 @@ __global__ void __launch_bounds__(256, 2) k_sgemm_pipe(const float* __restrict__
     const int slot = (int)(t % PG_S);
     const float* as = As + slot * A_STAGE;
     const float* bs = Bs + slot * B_STAGE;
-    const int kn = (int)min((uint32_t)PG_BK, k - t * PG_BK);  // the last tile may be partial
+    const uint32_t tk = (DUAL && t >= nt1) ? t - nt1 : t;      // k tile within its product
+    const int kn = (int)min((uint32_t)PG_BK, k - tk * PG_BK);  // the last tile may be partial
     if (kn == PG_BK) {
       // the next stage's copies go out between the two halves of the tile,
       // so no warp issues them while the others wait at the barrier
@@ -214,6 +234,41 @@ __global__ void __launch_bounds__(256, 2) k_sgemm_pipe(const float* __restrict__
       if (t + PG_S - 1 < ntiles) load_stage(t + PG_S - 1, (int)((t + PG_S - 1) % PG_S));
       cpa_commit();
       for (int kk = 0; kk < kn; kk++) kstep(as, bs, kk);
+    }
+    if constexpr (DUAL) {
+      if (t == nt1 - 1) {
+        // first product complete: store it as f32 into this thread's own
+        // outputs (read back by this thread in the epilogue), restart
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          const uint64_t gm = m0 + (i >> 2) * 64 + ty * 4 + (i & 3);
+#pragma unroll
+          for (int h = 0; h < TN / 4; h++) {
+            const uint32_t gn = n0 + h * 64 + tx * 4;
+            float v[4];
+            if constexpr (!EXACT) {
+              asm("mov.b64 {%0, %1}, %2;" : "=f"(v[0]), "=f"(v[1]) : "l"(accp[i][h * 2]));
+              asm("mov.b64 {%0, %1}, %2;" : "=f"(v[2]), "=f"(v[3]) : "l"(accp[i][h * 2 + 1]));
+            } else {
+#pragma unroll
+              for (int j = 0; j < 4; j++) v[j] = acc[i][h * 4 + j];
+            }
+            if (gm < m) {
+              if (V4OUT && gn + 3 < n) {
+                *reinterpret_cast<float4*>(C + gm * n + gn) = make_float4(v[0], v[1], v[2], v[3]);
+              } else {
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                  if (gn + j < n) C[gm * n + gn + j] = v[j];
+              }
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < TN; j++) acc[i][j] = 0.0f;
+#pragma unroll
+          for (int q = 0; q < TP; q++) accp[i][q] = 0ull;
+        }
+      }
     }
   }
   cpa_wait<0>();
@@ -306,44 +361,49 @@ __global__ void __launch_bounds__(256, 2) k_sgemm_pipe(const float* __restrict__
   if constexpr (REMOTE) __threadfence_system();  // peer stores visible before the kernel ends
 }
 
-template <int BN, bool EXACT, bool B16, bool V4OUT, bool REMOTE = false>
+template <int BN, bool EXACT, bool B16, bool V4OUT, bool REMOTE = false, bool DUAL = false>
 int launch_pipe_t(bgnn_ctx* ctx, const float* a, const float* b, uint32_t m, uint32_t k,
                   uint32_t n, const float* addend, const float* bias, int act, double act_param,
-                  float* out, const RemoteRows& rr = RemoteRows()) {
+                  float* out, const RemoteRows& rr = RemoteRows(), const float* a2 = nullptr,
+                  const float* b2 = nullptr) {
   constexpr size_t smem = pg_smem_bytes<BN>();
-  auto kern = k_sgemm_pipe<BN, EXACT, B16, V4OUT, REMOTE>;
+  auto kern = k_sgemm_pipe<BN, EXACT, B16, V4OUT, REMOTE, DUAL>;
   BGNN_CUDA(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)smem));
   dim3 grid((unsigned)((m + PG_BM - 1) / PG_BM), (n + BN - 1) / BN);
-  kern<<<grid, 256, smem, ctx->stream>>>(a, b, m, k, n, addend, bias, act, act_param, out, rr);
+  kern<<<grid, 256, smem, ctx->stream>>>(a, b, m, k, n, addend, bias, act, act_param, out, rr, a2,
+                                         b2);
   BGNN_LAUNCHED(ctx);
   return BGNN_OK;
 }
 
-// out = act(f32(f32(addend + a*b) + bias)), addend / bias optional
-template <bool EXACT>
+// out = act(f32(f32(addend + a*b) + bias)), addend / bias optional.
+// DUAL: out = act(f32(f32(f32(a*b) + a2*b2) + bias)) in one launch (addend
+// must be out).
+template <bool EXACT, bool DUAL = false>
 int launch_pipe(bgnn_ctx* ctx, const float* a, const float* b, uint32_t m, uint32_t k,
                 uint32_t n, const float* addend, const float* bias, int act, double act_param,
-                float* out) {
-  const bool b16 = (n % 4 == 0) && ((uintptr_t)b % 16 == 0);
+                float* out, const float* a2 = nullptr, const float* b2 = nullptr) {
+  const bool b16 = (n % 4 == 0) && ((uintptr_t)b % 16 == 0) && ((uintptr_t)b2 % 16 == 0);
   const bool v4 = (n % 4 == 0) && ((uintptr_t)out % 16 == 0) &&
                   (addend == nullptr || (uintptr_t)addend % 16 == 0);
+  const RemoteRows none;
   if (n <= 64) {
     if (b16)
-      return v4 ? launch_pipe_t<64, EXACT, true, true>(ctx, a, b, m, k, n, addend, bias, act,
-                                                       act_param, out)
-                : launch_pipe_t<64, EXACT, true, false>(ctx, a, b, m, k, n, addend, bias, act,
-                                                        act_param, out);
-    return launch_pipe_t<64, EXACT, false, false>(ctx, a, b, m, k, n, addend, bias, act,
-                                                  act_param, out);
+      return v4 ? launch_pipe_t<64, EXACT, true, true, false, DUAL>(
+                      ctx, a, b, m, k, n, addend, bias, act, act_param, out, none, a2, b2)
+                : launch_pipe_t<64, EXACT, true, false, false, DUAL>(
+                      ctx, a, b, m, k, n, addend, bias, act, act_param, out, none, a2, b2);
+    return launch_pipe_t<64, EXACT, false, false, false, DUAL>(
+        ctx, a, b, m, k, n, addend, bias, act, act_param, out, none, a2, b2);
   }
   if (b16)
-    return v4 ? launch_pipe_t<128, EXACT, true, true>(ctx, a, b, m, k, n, addend, bias, act,
-                                                      act_param, out)
-              : launch_pipe_t<128, EXACT, true, false>(ctx, a, b, m, k, n, addend, bias, act,
-                                                       act_param, out);
-  return launch_pipe_t<128, EXACT, false, false>(ctx, a, b, m, k, n, addend, bias, act, act_param,
-                                                 out);
+    return v4 ? launch_pipe_t<128, EXACT, true, true, false, DUAL>(
+                    ctx, a, b, m, k, n, addend, bias, act, act_param, out, none, a2, b2)
+              : launch_pipe_t<128, EXACT, true, false, false, DUAL>(
+                    ctx, a, b, m, k, n, addend, bias, act, act_param, out, none, a2, b2);
+  return launch_pipe_t<128, EXACT, false, false, false, DUAL>(
+      ctx, a, b, m, k, n, addend, bias, act, act_param, out, none, a2, b2);
 }
 
 }  // namespace
@@ -476,7 +536,13 @@ int bgnn_run_linear(bgnn_ctx* ctx, const float* a, const float* w, const float* 
   const bool dual = a2 != nullptr && w2 != nullptr;
   const bool exact = ctx->math == BGNN_MATH_EXACT;
   // SAGE pair: St = a2*w2 stored as f32 (the reference's Tensor), then
-  // f32(St + a*w) (+ bias, activation) in the second launch's epilogue
+  // f32(St + a*w) (+ bias, activation); one launch runs both products per
+  // output tile (k == 0 keeps two launches: the first writes St = 0)
+  if (dual && k > 0)
+    return exact ? launch_pipe<true, true>(ctx, a2, w2, m, k, n, out, bias, act, act_param, out,
+                                           a, w)
+                 : launch_pipe<false, true>(ctx, a2, w2, m, k, n, out, bias, act, act_param, out,
+                                            a, w);
   if (dual) {
     BGNN_TRY(exact ? launch_pipe<true>(ctx, a2, w2, m, k, n, nullptr, nullptr, 0, 0.0, out)
                    : launch_pipe<false>(ctx, a2, w2, m, k, n, nullptr, nullptr, 0, 0.0, out));
