@@ -781,7 +781,13 @@ def main():
     traffic = profile_traffic("aggregate_mean_f256_sage_rmat") if world == 1 else None
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak,
                 "unit": "GB/s", "frac": round(achieved / hbm_peak, 3), "traffic": traffic,
-                "kernel": "aggregate mean F=256 (light+heavy rows, one launch pair)",
+                "kernel": "aggregate mean F=256 (streaming kernel, one launch)",
+                # the gather model gives no credit for L2 hits, which R-MAT hubs
+                # get: the DRAM bytes ncu counts (traffic) over the same time
+                "dram_achieved": (round(traffic / (agg_avg_ms * 1e-3) / 1e9, 1)
+                                  if traffic else None),
+                "dram_frac": (round(traffic / (agg_avg_ms * 1e-3) / 1e9 / hbm_peak, 3)
+                              if traffic else None),
                 "bytes_model": "gather model: 4(N+1) + 4E + 4FE + 4FN",
                 "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
                 "launch_ms": round(agg_avg_ms, 3),
