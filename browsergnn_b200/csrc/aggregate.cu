@@ -498,7 +498,9 @@ __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint
       const float* wb = wbuf + slot * eps;
       const uint32_t base = k * (uint32_t)eps;
       const uint32_t cnt = min((uint32_t)eps, ne - base);
-      constexpr int UB = 16;
+      // 16-edge blocks with the lean epilogues; the generic one keeps 8 (its
+      // row-end path inlines the whole epilogue once per edge of the block)
+      constexpr int UB = EPI == EPI_ANY ? 8 : 16;
       uint32_t j = 0;
       for (; j + UB <= cnt; j += UB) {
         // issue the block's shared-memory reads first, then reduce in order
