@@ -160,18 +160,63 @@ __global__ void __launch_bounds__(256, 2) k_sgemm_pipe(const float* __restrict__
   // FAST: two adjacent columns share one packed fma.rn.f32x2 (two IEEE f32
   // fmas per instruction, each rounded exactly like fmaf), which halves the
   // FMA instructions the schedulers issue.  EXACT: the double-emulated step.
+  // ROWPAIR (FAST, 4 columns per thread): the packed pairs run down two
+  // adjacent rows instead, so the A pairs come straight from shared memory
+  // and only the 4 B values are duplicated (4 moves per k step, not 8).
   constexpr int TP = TN / 2;
+  constexpr bool ROWPAIR = !EXACT && TN == 4;
   float acc[8][TN];
   uint64_t accp[8][TP];  // FAST: (acc[i][2p], acc[i][2p+1]) packed
+  uint64_t accr[4][4];   // ROWPAIR: (acc[2p][j], acc[2p+1][j]) packed
+  auto zero = [&]() {
 #pragma unroll
-  for (int i = 0; i < 8; i++) {
+    for (int i = 0; i < 8; i++) {
 #pragma unroll
-    for (int j = 0; j < TN; j++) acc[i][j] = 0.0f;
+      for (int j = 0; j < TN; j++) acc[i][j] = 0.0f;
 #pragma unroll
-    for (int q = 0; q < TP; q++) accp[i][q] = 0ull;
-  }
+      for (int q = 0; q < TP; q++) accp[i][q] = 0ull;
+    }
+#pragma unroll
+    for (int p = 0; p < 4; p++)
+#pragma unroll
+      for (int j = 0; j < 4; j++) accr[p][j] = 0ull;
+  };
+  zero();
+  // this thread's outputs (row i, columns 4h..4h+3) from whichever layout
+  auto get4 = [&](int i, int h, float (&v)[4]) {
+    if constexpr (EXACT) {
+#pragma unroll
+      for (int j = 0; j < 4; j++) v[j] = acc[i][h * 4 + j];
+    } else if constexpr (ROWPAIR) {
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        float lo, hi;
+        asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(accr[i >> 1][j]));
+        v[j] = (i & 1) ? hi : lo;
+      }
+    } else {
+      asm("mov.b64 {%0, %1}, %2;" : "=f"(v[0]), "=f"(v[1]) : "l"(accp[i][h * 2]));
+      asm("mov.b64 {%0, %1}, %2;" : "=f"(v[2]), "=f"(v[3]) : "l"(accp[i][h * 2 + 1]));
+    }
+  };
 
   auto kstep = [&](const float* as, const float* bs, int kk) {
+    if constexpr (ROWPAIR) {
+      const ulonglong2 p0 = *reinterpret_cast<const ulonglong2*>(as + kk * AST + ty * 4);
+      const ulonglong2 p1 = *reinterpret_cast<const ulonglong2*>(as + kk * AST + 64 + ty * 4);
+      const uint64_t ap[4] = {p0.x, p0.y, p1.x, p1.y};
+      const float4 b0 = *reinterpret_cast<const float4*>(bs + kk * BN + tx * 4);
+      const float bw[4] = {b0.x, b0.y, b0.z, b0.w};
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        uint64_t bd;
+        asm("mov.b64 %0, {%1, %1};" : "=l"(bd) : "f"(bw[j]));
+#pragma unroll
+        for (int q = 0; q < 4; q++)
+          asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(accr[q][j]) : "l"(ap[q]), "l"(bd), "l"(accr[q][j]));
+      }
+      return;
+    }
     const float4 a0 = *reinterpret_cast<const float4*>(as + kk * AST + ty * 4);
     const float4 a1 = *reinterpret_cast<const float4*>(as + kk * AST + 64 + ty * 4);
     const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
@@ -246,13 +291,7 @@ __global__ void __launch_bounds__(256, 2) k_sgemm_pipe(const float* __restrict__
           for (int h = 0; h < TN / 4; h++) {
             const uint32_t gn = n0 + h * 64 + tx * 4;
             float v[4];
-            if constexpr (!EXACT) {
-              asm("mov.b64 {%0, %1}, %2;" : "=f"(v[0]), "=f"(v[1]) : "l"(accp[i][h * 2]));
-              asm("mov.b64 {%0, %1}, %2;" : "=f"(v[2]), "=f"(v[3]) : "l"(accp[i][h * 2 + 1]));
-            } else {
-#pragma unroll
-              for (int j = 0; j < 4; j++) v[j] = acc[i][h * 4 + j];
-            }
+            get4(i, h, v);
             if (gm < m) {
               if (V4OUT && gn + 3 < n) {
                 *reinterpret_cast<float4*>(C + gm * n + gn) = make_float4(v[0], v[1], v[2], v[3]);
@@ -263,16 +302,19 @@ __global__ void __launch_bounds__(256, 2) k_sgemm_pipe(const float* __restrict__
               }
             }
           }
-#pragma unroll
-          for (int j = 0; j < TN; j++) acc[i][j] = 0.0f;
-#pragma unroll
-          for (int q = 0; q < TP; q++) accp[i][q] = 0ull;
         }
+        zero();
       }
     }
   }
   cpa_wait<0>();
-  if constexpr (!EXACT) {
+  if constexpr (ROWPAIR) {
+#pragma unroll
+    for (int q = 0; q < 4; q++)
+#pragma unroll
+      for (int j = 0; j < 4; j++)
+        asm("mov.b64 {%0, %1}, %2;" : "=f"(acc[2 * q][j]), "=f"(acc[2 * q + 1][j]) : "l"(accr[q][j]));
+  } else if constexpr (!EXACT) {
 #pragma unroll
     for (int i = 0; i < 8; i++)
 #pragma unroll
