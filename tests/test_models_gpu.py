@@ -317,14 +317,17 @@ def test_training_mode_forward_runs(bg):
     assert not np.allclose(ev, t1)
 
 
-@pytest.mark.parametrize("n", [47, 256])
-def test_linear_add_is_sage_linear_split(bg, n):
+@pytest.mark.parametrize("exact", [True, False])
+@pytest.mark.parametrize("n", [47, 130, 256])
+def test_linear_add_is_sage_linear_split(bg, n, exact):
     """bgnn_linear (self product) then bgnn_linear_add (neighbour product
-    added to it) gives bgnn_sage_linear's bits."""
+    added to it) gives bgnn_sage_linear's bits: the fused launch (both
+    products per output tile) rounds exactly like the two launches, in both
+    math modes and for the 64- and 128-column tiles."""
     import torch
 
     rng = np.random.default_rng(n)
-    m, k = 700, 96
+    m, k = 700, 100
     x = rng.standard_normal((m, k)).astype(np.float32)
     agg = rng.standard_normal((m, k)).astype(np.float32)
     ws = (rng.standard_normal((k, n)) * 0.1).astype(np.float32)
@@ -332,7 +335,7 @@ def test_linear_add_is_sage_linear_split(bg, n):
     b = rng.standard_normal(n).astype(np.float32)
     d = {kk: _dev(v) for kk, v in dict(x=x, agg=agg, ws=ws, wn=wn, b=b).items()}
     ctx = bg.get_context()
-    ctx.set_math(True)
+    ctx.set_math(exact)
     try:
         st = torch.empty((m, n), dtype=torch.float32, device="cuda")
         out = torch.empty_like(st)
@@ -351,7 +354,26 @@ def test_linear_add_is_sage_linear_split(bg, n):
     nt_o = orc.matmul(agg, wn, m, k, n).reshape(m, n)
     comb = (st_o.astype(np.float64) + nt_o).astype(np.float32)
     comb = (comb.astype(np.float64) + b).astype(np.float32)
-    assert_bits_equal(out.cpu().numpy(), orc.relu(comb), "vs oracle")
+    if exact:
+        assert_bits_equal(out.cpu().numpy(), orc.relu(comb), "vs oracle")
+    else:
+        assert_close(out.cpu().numpy(), orc.relu(comb), "vs oracle")
+
+
+def test_sage_linear_k0(bg):
+    """No input features: both products are empty, the output is
+    act(f32(0 + 0) + bias) (the fused launch is skipped for k == 0)."""
+    import torch
+
+    m, n = 300, 40
+    b = np.linspace(-1, 1, n).astype(np.float32)
+    db = _dev(b)
+    out = torch.full((m, n), float("nan"), device="cuda")
+    dummy = torch.zeros(1, device="cuda")
+    ctx = bg.get_context()
+    ctx.call("bgnn_sage_linear", dummy.data_ptr(), dummy.data_ptr(), dummy.data_ptr(),
+             dummy.data_ptr(), m, 0, n, db.data_ptr(), 1, 0.0, out.data_ptr())
+    assert_bits_equal(out.cpu().numpy(), np.tile(np.maximum(b, 0), (m, 1)), "k == 0")
 
 
 def test_pinned_host_graphdata_overlaps_upload(bg):
