@@ -204,6 +204,19 @@ __device__ __forceinline__ void cp_async16(void* s, const void* g) {
   const unsigned sa = (unsigned)__cvta_generic_to_shared(s);
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(sa), "l"(g) : "memory");
 }
+// 32-bit shared-memory addresses for the streaming pipes' hot loops: the
+// ring is walked with stepped addresses instead of 64-bit index arithmetic
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ float lds_f32(uint32_t a) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];\n" : "=f"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ void cp_async16_sa(uint32_t sa, const void* g) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(sa), "l"(g) : "memory");
+}
 __device__ __forceinline__ void cp_async4(void* s, const void* g) {
   const unsigned sa = (unsigned)__cvta_generic_to_shared(s);
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(sa), "l"(g) : "memory");
@@ -387,10 +400,13 @@ __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint
         // ch divides the pipe width: the thread's chunk q never changes
         const float* src = a.x + f0 + QB * cq0;
         float* dst = sb + QB * cq0;
-        for (int j = cj0; j < cnt; j += cdj) {
-          if (CP == CP_A16)
-            cp_async16(dst + (size_t)j * swp, src + (int64_t)sid[j] * a.ld_x);
-          else
+        if (CP == CP_A16) {
+          uint32_t da = smem_u32(dst + (size_t)cj0 * swp);
+          const uint32_t dstep = (uint32_t)(cdj * swp) * 4u;
+          for (int j = cj0; j < cnt; j += cdj, da += dstep)
+            cp_async16_sa(da, src + (int64_t)sid[j] * a.ld_x);
+        } else {
+          for (int j = cj0; j < cnt; j += cdj)
             cp_async4(dst + (size_t)j * swp, src + (int64_t)sid[j] * a.ld_x);
         }
       } else {
@@ -494,7 +510,8 @@ __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint
         acc = step<OP>(acc, b[(size_t)j * swp], w);
       }
     } else if (consumer) {
-      const float* b = buf + (size_t)slot * eps * swp + ptid;
+      const uint32_t b32 = smem_u32(buf + (size_t)slot * eps * swp + ptid);
+      const uint32_t swp4 = (uint32_t)swp * 4u;
       const float* wb = wbuf + slot * eps;
       const uint32_t base = k * (uint32_t)eps;
       const uint32_t cnt = min((uint32_t)eps, ne - base);
@@ -505,9 +522,10 @@ __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint
       for (; j + UB <= cnt; j += UB) {
         // issue the block's shared-memory reads first, then reduce in order
         float v[UB], wr[UB];
+        uint32_t ra = b32 + j * swp4;
 #pragma unroll
-        for (int u = 0; u < UB; u++) {
-          v[u] = b[(size_t)(j + u) * swp];
+        for (int u = 0; u < UB; u++, ra += swp4) {
+          v[u] = lds_f32(ra);
           wr[u] = HAS_W ? wb[j + u] : 0.0f;
         }
         if (nxt >= base + j + UB) {  // no row ends inside this block
@@ -530,7 +548,7 @@ __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint
         float w = 0.0f;
         if (OP == OP_GCN) w = __fmul_rn(wb[j], dinv_r);
         if (OP == OP_SPMM || OP == OP_SPMM_X) w = wb[j];
-        acc = step<OP>(acc, b[(size_t)j * swp], w);
+        acc = step<OP>(acc, lds_f32(b32 + j * swp4), w);
       }
     }
   }
