@@ -272,13 +272,16 @@ class PartitionedSage:
             return ev
 
         nl = len(self.layers)
+        remote_done = [False] * nl  # layer li stored its rows into the peers' halos
         for li, lay in enumerate(self.layers):
             fin, fout = lay.inChannels, lay.outChannels
             ext, agg = self.ext[li], self.agg[li]
             out = self.ext[li + 1][:n_own] if li + 1 < nl else self.out
             act = 1 if li < nl - 1 else 0
             split = fout > 64
-            halo_ready = li > 0 and self.peer is not None  # filled by the previous epilogue
+            # halo rows already filled by the previous layer's epilogue (only
+            # when that layer ran the split, remote-storing linear)
+            halo_ready = li > 0 and remote_done[li - 1]
             remote_out = self.peer is not None and li + 1 < nl and split
             e0 = mark()
             # pack the rows the other ranks need, then start x * W_self (owned
@@ -305,6 +308,7 @@ class PartitionedSage:
                          part.world)
                 # every rank's stores land before anyone reads its halo rows
                 dist.all_reduce(self.flag, group=part.group)
+                remote_done[li] = True
             elif split:
                 main.wait_stream(self.side)
                 ctx.call("bgnn_linear_add", ptr(agg), ptr(lay.p("lin_neighbor")), n_own, fin,
@@ -322,7 +326,7 @@ class PartitionedSage:
 # ---------------------------------------------------------------------------
 # SpMM sweep (standalone CSR SpMM, scale-24 R-MAT, 2^28 edges)
 # ---------------------------------------------------------------------------
-def spmm_sweep(steps, warmup, hbm_peak):
+def spmm_sweep(steps, warmup, hbm_peak, parity=True):
     import torch
 
     import browsergnn_b200 as bg
@@ -352,6 +356,10 @@ def spmm_sweep(steps, warmup, hbm_peak):
     res = {"workload": f"spmm-rmat-s{scale}-{n}n-{e}e", "csr_build_ms": round(build_ms, 3)}
     per_f = {}
     gen = torch.Generator("cuda").manual_seed(seed + 1)
+    host_csr = None
+    if parity:
+        host_csr = (csr.rowPtr.cpu().numpy().view(np.uint32),
+                    csr.colIndices.cpu().numpy().view(np.uint32), csr.values.cpu().numpy())
     for f in (32, 64, 128, 256):
         x = torch.randn((n, f), device="cuda", generator=gen)
         out = torch.empty((n, f), device="cuda")
@@ -375,9 +383,91 @@ def spmm_sweep(steps, warmup, hbm_peak):
                          "hbm_frac_gather_model": round(gbs / hbm_peak, 3),
                          "compulsory_GBps": round((4 * (n + 1) + 8 * e + 8 * f * n)
                                                   / (ms * 1e-3) / 1e9, 1)}
+        if host_csr is not None and f in (32, 256):
+            per_f[str(f)]["parity"] = spmm_parity(host_csr, x, out, f, seed)
         del x, out
     res["per_feature_width"] = per_f
     g.close()
+    return res
+
+
+def partition_bit_identity(ei, n, e, seed, layers, part, got, device):
+    """Each rank's rows of the partitioned forward against the same rows of a
+    single-GPU forward of the whole graph on that rank's GPU: every row is
+    reduced in the same order on one GPU either way, so the bits must agree.
+    Returns the mismatch count summed over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from browsergnn_b200.graph import DeviceGraph
+
+    gen = torch.Generator("cuda").manual_seed(seed)
+    x_full = torch.randn((n, WIDTHS[0]), device="cuda", generator=gen)
+    dg = DeviceGraph(ei, e, n, n, device=device)
+    ref = sage_forward(layers, dg, x_full, None, None)
+    mine = ref[part.lo:part.hi]
+    bad = (mine.view(torch.int32) != got.view(torch.int32)) & ~(torch.isnan(mine) & torch.isnan(got))
+    counts = torch.tensor([int(bad.sum().item()), int(got.numel())], device="cuda",
+                          dtype=torch.int64)
+    dist.all_reduce(counts)
+    del ref, mine, x_full
+    dg.close()
+    return {"bit_identical_to_1gpu": bool(counts[0].item() == 0),
+            "differing_elements": int(counts[0].item()), "elements": int(counts[1].item()),
+            "checked": "every rank's rows against a single-GPU forward of the whole graph"}
+
+
+def spmm_parity(host_csr, x, out, f, seed):
+    """The SpMM output against the oracle's row-parallel wasmSpmm restatement
+    (same per-row order and roundings): every row at F = 32; at wider F every
+    heavy row (>= 256 entries, the hub and giant-row paths) plus 2,000,000
+    seeded random rows."""
+    from oracle import oracle as orc
+
+    rp, col, val = host_csr
+    n = rp.size - 1
+    t0 = time.perf_counter()
+    x_h = x.cpu().numpy()
+    if f <= 32:
+        rows = None
+        got = out.cpu().numpy()
+        what = f"all {n} rows"
+    else:
+        import torch
+
+        deg = np.diff(rp.astype(np.int64))
+        heavy = np.flatnonzero(deg >= 256).astype(np.uint32)
+        rnd = np.random.default_rng(seed).integers(0, n, 2_000_000).astype(np.uint32)
+        rows = np.unique(np.concatenate([heavy, rnd]))
+        idx = torch.from_numpy(rows.astype(np.int64)).to(out.device)
+        got = out.index_select(0, idx).cpu().numpy()
+        what = (f"{rows.size} rows: all {heavy.size} rows with >= 256 entries "
+                f"({int(deg[heavy].sum())} entries) + 2,000,000 random rows")
+    want = orc.spmm_rows(rp, col, val, x_h, f, rows=rows, num_rows=n, threads=0)
+    res = _parity(got, want.reshape(got.shape))
+    res["checked"] = what
+    res["oracle_seconds"] = round(time.perf_counter() - t0, 1)
+    return res
+
+
+def sage_oracle_parity(ei, n, e, x, weights, got_dev):
+    """The full 3-layer SAGE output (every row, every feature) against the
+    oracle's row-parallel restatement on all host threads."""
+    from oracle import oracle as orc
+
+    t0 = time.perf_counter()
+    got = got_dev.cpu().numpy()
+    ei_h = ei.cpu().numpy().view(np.uint32)
+    rp, so, _ = orc.dst_csr(ei_h, e, n)
+    del ei_h
+    h = x.cpu().numpy()
+    for li, (fin, fout) in enumerate(zip(WIDTHS[:-1], WIDTHS[1:])):
+        lw = weights[li]
+        h = orc.sage_forward_csr(rp, so, n, h, fin, "mean", lw["lin_neighbor"], lw["lin_self"],
+                                 lw["bias"], fout, relu=li < 2, threads=0)
+    res = _parity(got, h.reshape(got.shape))
+    res["checked"] = f"full output [{n}, {WIDTHS[-1]}] of the 3-layer forward"
+    res["oracle_seconds"] = round(time.perf_counter() - t0, 1)
     return res
 
 
@@ -568,7 +658,8 @@ def profile_case(kind):
     small    : R-MAT 1,000,000 nodes / 25,000,000 edges, F=256: one mean
                aggregation, then one SAGE linear 256 -> 256 (two SGEMM launches)
     full-agg : the benchmark graph (2,450,000 / 62,000,000), F=256 mean
-               aggregation twice (capture the second)."""
+               aggregation twice (capture the second)
+    csr      : SparseCSR.fromCOO of the SpMM workload (2^28 entries), twice."""
     import torch
 
     import browsergnn_b200 as bg
@@ -576,13 +667,28 @@ def profile_case(kind):
     from browsergnn_b200.backend import ptr
     from browsergnn_b200.graph import DeviceGraph
 
+    bg.init_browsergnn()
+    ctx = bg.get_context()
+    if kind == "csr":
+        # SparseCSR.fromCOO of the SpMM workload's 2^28 entries, twice
+        n, e = 1 << synth.SPMM_SCALE, synth.SPMM_E
+        ei = synth.rmat_edges_gpu(synth.SPMM_SCALE, n, e, synth.seed_for(5))
+        vals = torch.ones(e, device="cuda")
+        for _ in range(2):
+            a0 = torch.cuda.Event(enable_timing=True)
+            a1 = torch.cuda.Event(enable_timing=True)
+            a0.record()
+            csr = bg.SparseCSR.fromCOO(bg.SparseCOO(ei[:e], ei[e:], vals, (n, n)))
+            a1.record()
+            torch.cuda.synchronize()
+            print(f"fromCOO {e} entries: {a0.elapsed_time(a1):.3f} ms")
+            del csr
+        return
     if kind == "small":
         scale, n, e = 20, 1_000_000, 25_000_000
     else:
         scale, n, e = synth.SAGE_SCALE, synth.SAGE_N, synth.SAGE_E
     f = 256
-    bg.init_browsergnn()
-    ctx = bg.get_context()
     ei = synth.rmat_edges_gpu(scale, n, e, synth.seed_for(4))
     dg = DeviceGraph(ei, e, n, n)
     gen = torch.Generator("cuda").manual_seed(1)
@@ -622,7 +728,7 @@ def run_reference(args, rank, world):
         cpu_sample_forward(threads, repeats=1)
     vals, secs = [], []
     for _ in range(args.steps):
-        v, desc, e_s, t = cpu_sample_forward(threads, repeats=1)
+        v, desc, e_s, t = cpu_sample_forward(threads, repeats=3)
         vals.append(v)
         secs.append(t)
     value = statistics.mean(vals)
@@ -653,11 +759,13 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-spmm", action="store_true")
     ap.add_argument("--no-small", action="store_true")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="skip the full-size output checks (oracle at N=1, N=1 bits at N>1)")
     ap.add_argument("--peer-stores", action="store_true",
                     help="N>1: layers 2-3 get their halo rows from the previous layer's epilogue "
                          "storing into the peers' buffers instead of the all-to-all (bit-identical; "
                          "faster at 2 GPUs, slower at 8: 16-byte peer stores use NVLink poorly)")
-    ap.add_argument("--profile", choices=["small", "full-agg"], default=None,
+    ap.add_argument("--profile", choices=["small", "full-agg", "csr"], default=None,
                     help="run one profiling case for ncu and exit")
     args = ap.parse_args()
     if args.profile:
@@ -745,6 +853,8 @@ def main():
     barrier()
     clocks = sampler.stop()
     launches = (ctx.launches - l0)
+    final = step()  # one more untimed forward: the output the parity check reads
+    torch.cuda.synchronize()
     ms_total = start.elapsed_time(stop)
     if world > 1:
         t = torch.tensor([ms_total], device="cuda")
@@ -824,17 +934,29 @@ def main():
                "d2h_bytes_per_step": int(res.numel() * 4), "ms_per_step": round(1000 * e2e_s, 3),
                "includes": "H2D of features and edge index, device CSR build, 3 layers, D2H"}
 
+    # parity at full size: N=1 against the oracle (every output element);
+    # N>1 bit for bit against a single-GPU forward of the whole graph, which
+    # every rank runs on its own GPU for its own rows
+    parity = None
+    if not args.no_parity:
+        if world == 1:
+            parity = sage_oracle_parity(ei, n, e, x, weights, final)
+        else:
+            parity = partition_bit_identity(ei, n, e, seed, layers, part, final, local)
+    del final
+
     cpu = None
     if not args.no_cpu and rank == 0 and world == 1:
         threads = os.cpu_count() or 1
-        v, desc, _, _ = cpu_sample_forward(threads)
-        cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": desc}
+        v, desc, _, _ = cpu_sample_forward(threads, repeats=3)
+        cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": desc + " (best of 3)"}
 
     spmm = None
     if not args.no_spmm and world == 1:
         del dg
         torch.cuda.empty_cache()
-        spmm = spmm_sweep(max(3, args.steps // 2), 3, hbm_peak)
+        spmm = spmm_sweep(max(3, args.steps // 2), 3, hbm_peak, parity=not args.no_parity)
     small = None
     if not args.no_small and world == 1:
         small = small_workloads(max(3, args.steps), 3)
@@ -853,6 +975,7 @@ def main():
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
             "clocks": clocks, "gpu_launches": launches,
             "phase_ms_max_over_ranks": phase_ms,
+            "parity": parity,
         }
         if part is not None:
             line["config"]["halo_rows_rank0"] = part.n_halo

@@ -155,6 +155,27 @@ void orc_spmm(const uint32_t* row_ptr, const uint32_t* col, const float* val, co
   }
 }
 
+/* wasmSpmm (src/backend/wasm/index.ts:342-383) for a list of rows, row-parallel:
+ * every row is computed exactly as in orc_spmm (CSR order, f32 store after
+ * each double step), so the bits are the same.  rows NULL: rows 0..nrows-1.
+ * out is [nrows, nf] in the order of the list. */
+void orc_spmm_rows(const uint32_t* row_ptr, const uint32_t* col, const float* val,
+                   const float* dense, int64_t nf, const uint32_t* rows, int64_t nrows,
+                   int threads, float* out) {
+  const int nt = pick_threads(threads);
+#pragma omp parallel for schedule(dynamic, 64) num_threads(nt)
+  for (int64_t q = 0; q < nrows; q++) {
+    const int64_t i = rows ? (int64_t)rows[q] : q;
+    float* o = out + q * nf;
+    for (int64_t f = 0; f < nf; f++) o[f] = 0.0f;
+    for (uint32_t j = row_ptr[i]; j < row_ptr[i + 1]; j++) {
+      const double v = (double)val[j];
+      const float* d = dense + (int64_t)col[j] * nf;
+      for (int64_t f = 0; f < nf; f++) o[f] = (float)((double)o[f] + v * (double)d[f]);
+    }
+  }
+}
+
 /* SparseCOO.matmul, src/core/sparse.ts:138-159: COO (edge) order. */
 void orc_coo_spmm(const uint32_t* rows, const uint32_t* cols, const float* vals, int64_t nnz,
                   int64_t m, const float* dense, int64_t k, float* out) {

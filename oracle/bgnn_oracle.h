@@ -117,6 +117,11 @@ int orc_sage_forward_csr(const uint32_t* row_ptr, const uint32_t* src_of, int64_
                          int relu, int threads, float* out);
 void orc_matmul_par(const float* a, const float* b, int64_t m, int64_t k, int64_t n,
                     int threads, float* out);
+/* wasmSpmm for a list of rows (NULL: rows 0..nrows-1), row-parallel, same
+ * bits as orc_spmm; out is [nrows, nf] in list order. */
+void orc_spmm_rows(const uint32_t* row_ptr, const uint32_t* col, const float* val,
+                   const float* dense, int64_t nf, const uint32_t* rows, int64_t nrows,
+                   int threads, float* out);
 
 /* ---- model zoo: src/nn/linear.ts, src/nn/activation.ts, src/core/tensor.ts,
  *      and the three models under src/models/ ------------------------------ */

@@ -55,6 +55,7 @@ def _declare(L):
         "orc_add": (v, [_F, _F, _I64, _F]),
         "orc_spmv": (v, [_U, _U, _F, _F, _I64, _F]),
         "orc_spmm": (v, [_U, _U, _F, _F, _I64, _I64, _F]),
+        "orc_spmm_rows": (v, [_U, _U, _F, _F, _I64, _U, _I64, ctypes.c_int, _F]),
         "orc_coo_spmm": (v, [_U, _U, _F, _I64, _I64, _F, _I64, _F]),
         "orc_coo_to_csr": (ctypes.c_int, [_U, _U, _F, _I64, _I64, _U, _U, _F]),
         "orc_gcn_norm": (v, [_U, _I64, _I64, ctypes.c_int, _F]),
@@ -207,6 +208,23 @@ def spmm(row_ptr, col, val, dense, num_rows, nf):
     out = np.empty(num_rows * nf, np.float32)
     lib().orc_spmm(_pu(row_ptr), _pu(col), _pf(val), _pf(dense), num_rows, nf, _pf(out))
     return out
+
+
+def spmm_rows(row_ptr, col, val, dense, nf, rows=None, num_rows=None, threads=0):
+    """wasmSpmm for the listed rows (all rows when rows is None), row-parallel
+    on `threads` host threads (0: all); [len(rows), nf] in list order."""
+    row_ptr, col, val, dense = _u(row_ptr), _u(col), _f(val), _f(dense)
+    if rows is None:
+        nrows = int(num_rows if num_rows is not None else row_ptr.size - 1)
+        rp = None
+    else:
+        rows = _u(rows)
+        nrows = int(rows.size)
+        rp = _pu(rows)
+    out = np.empty(max(nrows * nf, 1), np.float32)
+    lib().orc_spmm_rows(_pu(row_ptr), _pu(col), _pf(val), _pf(dense), nf, rp, nrows, threads,
+                        _pf(out))
+    return out[: nrows * nf]
 
 
 def coo_spmm(rows, cols, vals, m, dense, k):

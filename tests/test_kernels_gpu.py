@@ -254,7 +254,7 @@ def test_matmul(bg, torch, exact, mkn):
         if exact:
             assert_bits_equal(got, want, "matmul exact")
         else:
-            assert_close(got, want, "matmul fast", rtol=1e-5, atol=1e-5)
+            assert_close(got, want, "matmul fast")
     finally:
         ctx.set_math(False)
 
