@@ -121,17 +121,15 @@ __device__ __forceinline__ void dev_raise(int* err, int code, uint64_t info, int
 // ---------------------------------------------------------------------------
 // exclusive prefix sum of n uint32 values (in may equal out)
 int bgnn_exclusive_scan(bgnn_ctx* ctx, const uint32_t* in, uint32_t* out, uint64_t n);
-// stable LSD radix sort of 32-bit keys carrying 32-bit values.  vals_in NULL
-// means the identity (0,1,2,...).  key_bits: number of low key bits to sort.
-// Results land in keys_out / vals_out (keys_out may be NULL when only the
-// permutation is wanted).
-int bgnn_radix_sort_pairs(bgnn_ctx* ctx, const uint32_t* keys_in, const uint32_t* vals_in,
-                          uint64_t n, int key_bits, uint32_t* keys_out, uint32_t* vals_out);
+// Stable LSD radix sort (8-bit digits) of 32-bit keys carrying up to two
+// 32-bit payload streams.  Payload 0 is p0_in, or the item's input index
+// when ident0 != 0 (p0_in NULL); payload 1 is p1_in (NULL: none; needs
+// payload 0).  key_bits: number of low key bits to sort.  keys_out may be
+// NULL when the sorted keys are not wanted.
+int bgnn_radix_sort(bgnn_ctx* ctx, const uint32_t* keys_in, uint64_t n, int key_bits,
+                    const uint32_t* p0_in, int ident0, const uint32_t* p1_in, uint32_t* keys_out,
+                    uint32_t* p0_out, uint32_t* p1_out);
 int bgnn_bits_for(uint64_t max_value);
-// out[i] = src[idx[i]]
-int bgnn_gather_u32(bgnn_ctx* ctx, const uint32_t* src, const uint32_t* idx, uint64_t n,
-                    uint32_t* out);
-int bgnn_gather_f32(bgnn_ctx* ctx, const float* src, const uint32_t* idx, uint64_t n, float* out);
 int bgnn_iota(bgnn_ctx* ctx, uint32_t* out, uint64_t n);
 int bgnn_check_device_error(bgnn_ctx* ctx);
 

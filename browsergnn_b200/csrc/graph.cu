@@ -239,10 +239,10 @@ int bgnn_graph_build(bgnn_ctx* ctx, const uint32_t* src, const uint32_t* dst, ui
   }
   g->has_self_loops = (int)(hbuf[0] & 0xffffffffull) != 0;
   BGNN_TRY(counts_to_rowptr(ctx, g->row_ptr, n_dst));
-  // stable sort of edge ids by destination: each row keeps its edges in COO order
+  // stable sort by destination carrying each edge's id and source: every row
+  // keeps its edges in COO order
   const int bits = n_dst > 1 ? bgnn_bits_for(n_dst - 1) : 0;
-  BGNN_TRY(bgnn_radix_sort_pairs(ctx, dst, nullptr, E, bits, nullptr, g->eid));
-  BGNN_TRY(bgnn_gather_u32(ctx, src, g->eid, E, g->src_of));
+  BGNN_TRY(bgnn_radix_sort(ctx, dst, E, bits, nullptr, 1, src, nullptr, g->eid, g->src_of));
   BGNN_TRY(build_schedule(ctx, g));
   return BGNN_OK;
 }
@@ -473,24 +473,26 @@ extern "C" int bgnn_coo_to_csr_dev(bgnn_ctx* ctx, const uint32_t* rows, const ui
                           hb < nnz ? "column" : "row", hb < nnz ? hb : hb - nnz);
   BGNN_TRY(counts_to_rowptr(ctx, row_ptr, num_rows));
   if (nnz == 0) return BGNN_OK;
-  DevTmp perm1, perm2, rows_p;
-  BGNN_TRY(bgnn_tmp_alloc(ctx, perm1, nnz * 4));
-  BGNN_TRY(bgnn_tmp_alloc(ctx, perm2, nnz * 4));
-  BGNN_TRY(bgnn_tmp_alloc(ctx, rows_p, nnz * 4));
+  // column pass: stable sort by column carrying each entry's row (and value);
+  // row pass: stable sort of that order by row carrying the columns (and
+  // values).  The result is sorted by (row, col) with ties in input order.
+  const bool want_vals = values != nullptr && val_out != nullptr;
+  const uint32_t* vbits = reinterpret_cast<const uint32_t*>(values);
+  DevTmp cols_c, rows_c, vals_c;
+  BGNN_TRY(bgnn_tmp_alloc(ctx, cols_c, nnz * 4));
+  BGNN_TRY(bgnn_tmp_alloc(ctx, rows_c, nnz * 4));
+  if (want_vals) BGNN_TRY(bgnn_tmp_alloc(ctx, vals_c, nnz * 4));
   const int cbits = num_cols > 1 ? bgnn_bits_for(num_cols - 1) : 0;
   const int rbits = num_rows > 1 ? bgnn_bits_for(num_rows - 1) : 0;
-  BGNN_TRY(bgnn_radix_sort_pairs(ctx, cols, nullptr, nnz, cbits, nullptr, perm1.as<uint32_t>()));
-  BGNN_TRY(bgnn_gather_u32(ctx, rows, perm1.as<uint32_t>(), nnz, rows_p.as<uint32_t>()));
-  BGNN_TRY(bgnn_radix_sort_pairs(ctx, rows_p.as<uint32_t>(), perm1.as<uint32_t>(), nnz, rbits,
-                                 nullptr, perm2.as<uint32_t>()));
-  BGNN_TRY(bgnn_gather_u32(ctx, cols, perm2.as<uint32_t>(), nnz, col_out));
-  if (val_out) {
-    if (values) {
-      BGNN_TRY(bgnn_gather_f32(ctx, values, perm2.as<uint32_t>(), nnz, val_out));
-    } else {
-      k_fill_ones<<<grid_for(ctx, nnz, 256), 256, 0, ctx->stream>>>(val_out, nnz);
-      BGNN_LAUNCHED(ctx);
-    }
+  BGNN_TRY(bgnn_radix_sort(ctx, cols, nnz, cbits, rows, 0, want_vals ? vbits : nullptr,
+                           cols_c.as<uint32_t>(), rows_c.as<uint32_t>(),
+                           want_vals ? vals_c.as<uint32_t>() : nullptr));
+  BGNN_TRY(bgnn_radix_sort(ctx, rows_c.as<uint32_t>(), nnz, rbits, cols_c.as<uint32_t>(), 0,
+                           want_vals ? vals_c.as<uint32_t>() : nullptr, nullptr, col_out,
+                           want_vals ? reinterpret_cast<uint32_t*>(val_out) : nullptr));
+  if (val_out && !values) {
+    k_fill_ones<<<grid_for(ctx, nnz, 256), 256, 0, ctx->stream>>>(val_out, nnz);
+    BGNN_LAUNCHED(ctx);
   }
   return BGNN_OK;
 }

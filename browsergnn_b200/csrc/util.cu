@@ -1,4 +1,4 @@
-// Device primitives: exclusive scan, stable LSD radix sort, gathers.
+// Device primitives: exclusive scan, stable LSD radix sort.
 //
 // The CSR builds need a *stable* ordering (each destination row keeps its
 // edges in COO order, SparseCSR.fromCOO keeps ties in input order), so the
@@ -94,21 +94,32 @@ __global__ void __launch_bounds__(TPB) k_radix_hist(const uint32_t* __restrict__
   hist[(uint64_t)threadIdx.x * num_tiles + blockIdx.x] = h[threadIdx.x];
 }
 
-// One stable counting pass over 8 key bits.  Warp w of a tile owns items
-// [w*512, w*512+512) in input order and ranks them 32 at a time; the ranks
-// plus per-(warp,digit) running counts give every item its position among
-// the tile's items of the same digit, in input order.
-__global__ void __launch_bounds__(TPB) k_radix_scatter(const uint32_t* __restrict__ keys_in,
-                                                       const uint32_t* __restrict__ vals_in,
-                                                       uint64_t n, int shift, uint32_t num_tiles,
-                                                       const uint32_t* __restrict__ offs,
-                                                       uint32_t* __restrict__ keys_out,
-                                                       uint32_t* __restrict__ vals_out) {
+// One stable counting pass over 8 key bits, carrying NP payload words per
+// item.  Warp w of a tile owns items [w*512, w*512+512) in input order and
+// ranks them 32 at a time; the ranks plus per-(warp,digit) running counts give
+// every item its position among the tile's items of the same digit, in input
+// order.  The tile is then regrouped by digit in shared memory (keys and
+// payloads, the payloads read from global memory only at that point, in
+// input order), and each digit's run is written to its global position,
+// consecutive threads on consecutive positions.  The tile's 256 global digit
+// offsets are read once into shared memory: reading them per item from the
+// digit-major table (one cache line per digit, 256 lines per tile) missed L1
+// and cost a random L2 read per item.
+// ident0: payload 0 is the item's input index (p0_in unused).
+template <int NP>
+__global__ void __launch_bounds__(TPB) k_radix_scatter(
+    const uint32_t* __restrict__ keys_in, const uint32_t* __restrict__ p0_in,
+    const uint32_t* __restrict__ p1_in, int ident0, uint64_t n, int shift, uint32_t num_tiles,
+    const uint32_t* __restrict__ offs, uint32_t* __restrict__ keys_out,
+    uint32_t* __restrict__ p0_out, uint32_t* __restrict__ p1_out) {
   __shared__ uint32_t whist[WARPS][RADIX];
   __shared__ uint32_t tile_off[RADIX];
+  __shared__ uint32_t gbase[RADIX];  // global position of the tile's digit-d run, minus tile_off[d]
   __shared__ uint32_t wsum[WARPS];
-  __shared__ uint32_t sk[TILE];
-  __shared__ uint32_t sv[TILE];
+  extern __shared__ uint32_t rs_dyn[];
+  uint32_t* sk = rs_dyn;             // [TILE] keys grouped by digit
+  uint32_t* sp0 = rs_dyn + TILE;     // [TILE] payload 0 (NP >= 1)
+  uint32_t* sp1 = rs_dyn + 2 * TILE; // [TILE] payload 1 (NP == 2)
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   for (int i = threadIdx.x; i < WARPS * RADIX; i += TPB) (&whist[0][0])[i] = 0;
   __syncthreads();
@@ -116,13 +127,12 @@ __global__ void __launch_bounds__(TPB) k_radix_scatter(const uint32_t* __restric
   const uint64_t tile_base = (uint64_t)blockIdx.x * TILE;
   const uint64_t wbase = tile_base + (uint64_t)w * (32 * ROUNDS);
   const unsigned lt_mask = (1u << lane) - 1u;
-  uint32_t key[ROUNDS], val[ROUNDS], loc[ROUNDS];
+  uint32_t key[ROUNDS], loc[ROUNDS];
 #pragma unroll
   for (int r = 0; r < ROUNDS; r++) {
     const uint64_t i = wbase + (uint64_t)r * 32 + lane;
     const bool valid = i < n;
     const uint32_t k = valid ? keys_in[i] : 0u;
-    const uint32_t v = valid ? (vals_in ? vals_in[i] : (uint32_t)i) : 0u;
     const uint32_t d = valid ? ((k >> shift) & (RADIX - 1)) : (uint32_t)RADIX;
     const unsigned peers = __match_any_sync(FULL, d);
     const int leader = __ffs(peers) - 1;
@@ -134,7 +144,6 @@ __global__ void __launch_bounds__(TPB) k_radix_scatter(const uint32_t* __restric
     b = __shfl_sync(FULL, b, leader);
     __syncwarp();
     key[r] = k;
-    val[r] = v;
     loc[r] = valid ? (b + (uint32_t)__popc(peers & lt_mask)) : 0xffffffffu;
   }
   __syncthreads();
@@ -154,7 +163,9 @@ __global__ void __launch_bounds__(TPB) k_radix_scatter(const uint32_t* __restric
     __syncthreads();
     uint32_t wb = 0;
     for (int ww = 0; ww < w; ww++) wb += wsum[ww];
-    tile_off[d] = wb + inc - run;
+    const uint32_t toff = wb + inc - run;
+    tile_off[d] = toff;
+    gbase[d] = offs[(uint64_t)d * num_tiles + blockIdx.x] - toff;
   }
   __syncthreads();
 #pragma unroll
@@ -162,8 +173,10 @@ __global__ void __launch_bounds__(TPB) k_radix_scatter(const uint32_t* __restric
     if (loc[r] != 0xffffffffu) {
       const uint32_t d = (key[r] >> shift) & (RADIX - 1);
       const uint32_t p = tile_off[d] + whist[w][d] + loc[r];
+      const uint64_t i = wbase + (uint64_t)r * 32 + lane;
       sk[p] = key[r];
-      sv[p] = val[r];
+      if (NP >= 1) sp0[p] = ident0 ? (uint32_t)i : p0_in[i];
+      if (NP >= 2) sp1[p] = p1_in[i];
     }
   }
   __syncthreads();
@@ -171,25 +184,11 @@ __global__ void __launch_bounds__(TPB) k_radix_scatter(const uint32_t* __restric
   const uint32_t count = rem < (uint64_t)TILE ? (uint32_t)rem : (uint32_t)TILE;
   for (uint32_t p = threadIdx.x; p < count; p += TPB) {
     const uint32_t k = sk[p];
-    const uint32_t d = (k >> shift) & (RADIX - 1);
-    const uint64_t g = (uint64_t)offs[(uint64_t)d * num_tiles + blockIdx.x] + (p - tile_off[d]);
+    const uint64_t g = (uint64_t)gbase[(k >> shift) & (RADIX - 1)] + p;
     if (keys_out) keys_out[g] = k;
-    vals_out[g] = sv[p];
+    if (NP >= 1) p0_out[g] = sp0[p];
+    if (NP >= 2) p1_out[g] = sp1[p];
   }
-}
-
-__global__ void k_gather_u32(const uint32_t* __restrict__ src, const uint32_t* __restrict__ idx,
-                             uint64_t n, uint32_t* __restrict__ out) {
-  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
-       i += (uint64_t)gridDim.x * blockDim.x)
-    out[i] = src[idx[i]];
-}
-
-__global__ void k_gather_f32(const float* __restrict__ src, const uint32_t* __restrict__ idx,
-                             uint64_t n, float* __restrict__ out) {
-  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
-       i += (uint64_t)gridDim.x * blockDim.x)
-    out[i] = src[idx[i]];
 }
 
 __global__ void k_iota(uint32_t* out, uint64_t n) {
@@ -257,68 +256,85 @@ int bgnn_bits_for(uint64_t max_value) {
   return b;
 }
 
-int bgnn_radix_sort_pairs(bgnn_ctx* ctx, const uint32_t* keys_in, const uint32_t* vals_in,
-                          uint64_t n, int key_bits, uint32_t* keys_out, uint32_t* vals_out) {
+int bgnn_radix_sort(bgnn_ctx* ctx, const uint32_t* keys_in, uint64_t n, int key_bits,
+                    const uint32_t* p0_in, int ident0, const uint32_t* p1_in, uint32_t* keys_out,
+                    uint32_t* p0_out, uint32_t* p1_out) {
   if (n == 0) return BGNN_OK;
   if (n > 0xffffffffull)
     return bgnn_set_error(ctx, BGNN_ERR_UNSUPPORTED, "radix sort limited to 2^32-1 items");
+  const bool has0 = p0_in != nullptr || ident0;
+  const bool has1 = p1_in != nullptr;
+  if (has1 && !has0)
+    return bgnn_set_error(ctx, BGNN_ERR_INVALID_ARG, "radix sort: payload 1 without payload 0");
+  const int np = (has0 ? 1 : 0) + (has1 ? 1 : 0);
   const int passes = (key_bits + 7) / 8;
-  if (passes == 0) {
-    if (vals_in)
-      BGNN_CUDA(ctx, cudaMemcpyAsync(vals_out, vals_in, n * 4, cudaMemcpyDeviceToDevice,
-                                     ctx->stream));
-    else {
-      k_iota<<<grid_for(ctx, n, 256), 256, 0, ctx->stream>>>(vals_out, n);
+  if (passes == 0) {  // every key equal: the input order is the sorted order
+    if (ident0) {
+      k_iota<<<grid_for(ctx, n, 256), 256, 0, ctx->stream>>>(p0_out, n);
       BGNN_LAUNCHED(ctx);
+    } else if (p0_in) {
+      BGNN_CUDA(ctx, cudaMemcpyAsync(p0_out, p0_in, n * 4, cudaMemcpyDeviceToDevice, ctx->stream));
     }
+    if (p1_in)
+      BGNN_CUDA(ctx, cudaMemcpyAsync(p1_out, p1_in, n * 4, cudaMemcpyDeviceToDevice, ctx->stream));
     if (keys_out)
       BGNN_CUDA(ctx, cudaMemcpyAsync(keys_out, keys_in, n * 4, cudaMemcpyDeviceToDevice,
                                      ctx->stream));
     return BGNN_OK;
   }
   const uint64_t tiles = (n + TILE - 1) / TILE;
-  DevTmp hist, kb0, kb1, vb0, vb1;
+  DevTmp hist, kb[2], pb0[2], pb1[2];
   BGNN_TRY(bgnn_tmp_alloc(ctx, hist, tiles * RADIX * sizeof(uint32_t)));
-  BGNN_TRY(bgnn_tmp_alloc(ctx, kb0, n * 4));
-  BGNN_TRY(bgnn_tmp_alloc(ctx, kb1, n * 4));
-  BGNN_TRY(bgnn_tmp_alloc(ctx, vb0, n * 4));
-  BGNN_TRY(bgnn_tmp_alloc(ctx, vb1, n * 4));
+  if (passes > 1) {
+    for (int b = 0; b < 2 && b < passes - 1; b++) {
+      BGNN_TRY(bgnn_tmp_alloc(ctx, kb[b], n * 4));
+      if (has0) BGNN_TRY(bgnn_tmp_alloc(ctx, pb0[b], n * 4));
+      if (has1) BGNN_TRY(bgnn_tmp_alloc(ctx, pb1[b], n * 4));
+    }
+  }
+  const size_t dyn = (size_t)(1 + np) * TILE * sizeof(uint32_t);
+  static_assert(TILE * 4 * 3 + (WARPS * RADIX + 2 * RADIX + WARPS) * 4 <= 227 * 1024,
+                "radix tile fits in shared memory");
   const uint32_t* kin = keys_in;
-  const uint32_t* vin = vals_in;
-  uint32_t* kbuf[2] = {kb0.as<uint32_t>(), kb1.as<uint32_t>()};
-  uint32_t* vbuf[2] = {vb0.as<uint32_t>(), vb1.as<uint32_t>()};
+  const uint32_t* pin0 = p0_in;
+  const uint32_t* pin1 = p1_in;
+  int ident = ident0;
   for (int p = 0; p < passes; p++) {
     const int shift = 8 * p;
     const bool last = p == passes - 1;
-    uint32_t* kout = last ? keys_out : kbuf[p & 1];
-    uint32_t* vout = last ? vals_out : vbuf[p & 1];
+    uint32_t* kout = last ? keys_out : kb[p & 1].as<uint32_t>();
+    uint32_t* pout0 = last ? p0_out : pb0[p & 1].as<uint32_t>();
+    uint32_t* pout1 = last ? p1_out : pb1[p & 1].as<uint32_t>();
     k_radix_hist<<<(unsigned)tiles, TPB, 0, ctx->stream>>>(kin, n, shift, (uint32_t)tiles,
                                                             hist.as<uint32_t>());
     BGNN_LAUNCHED(ctx);
     BGNN_TRY(bgnn_exclusive_scan(ctx, hist.as<uint32_t>(), hist.as<uint32_t>(), tiles * RADIX));
-    // the last pass may skip writing keys when the caller does not want them
-    k_radix_scatter<<<(unsigned)tiles, TPB, 0, ctx->stream>>>(
-        kin, vin, n, shift, (uint32_t)tiles, hist.as<uint32_t>(), kout, vout);
+    // the last pass skips writing keys when the caller does not want them
+    switch (np) {
+      case 0:
+        k_radix_scatter<0><<<(unsigned)tiles, TPB, dyn, ctx->stream>>>(
+            kin, nullptr, nullptr, 0, n, shift, (uint32_t)tiles, hist.as<uint32_t>(), kout,
+            nullptr, nullptr);
+        break;
+      case 1:
+        k_radix_scatter<1><<<(unsigned)tiles, TPB, dyn, ctx->stream>>>(
+            kin, pin0, nullptr, ident, n, shift, (uint32_t)tiles, hist.as<uint32_t>(), kout,
+            pout0, nullptr);
+        break;
+      default:
+        BGNN_CUDA(ctx, cudaFuncSetAttribute(k_radix_scatter<2>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn));
+        k_radix_scatter<2><<<(unsigned)tiles, TPB, dyn, ctx->stream>>>(
+            kin, pin0, pin1, ident, n, shift, (uint32_t)tiles, hist.as<uint32_t>(), kout, pout0,
+            pout1);
+        break;
+    }
     BGNN_LAUNCHED(ctx);
-    kin = kout ? kout : kin;  // (kout is only null on the last pass)
-    vin = vout;
+    kin = kout;  // (kout is only null on the last pass)
+    pin0 = pout0;
+    pin1 = pout1;
+    ident = 0;
   }
-  return BGNN_OK;
-}
-
-int bgnn_gather_u32(bgnn_ctx* ctx, const uint32_t* src, const uint32_t* idx, uint64_t n,
-                    uint32_t* out) {
-  if (n == 0) return BGNN_OK;
-  k_gather_u32<<<grid_for(ctx, n, 256), 256, 0, ctx->stream>>>(src, idx, n, out);
-  BGNN_LAUNCHED(ctx);
-  return BGNN_OK;
-}
-
-int bgnn_gather_f32(bgnn_ctx* ctx, const float* src, const uint32_t* idx, uint64_t n,
-                    float* out) {
-  if (n == 0) return BGNN_OK;
-  k_gather_f32<<<grid_for(ctx, n, 256), 256, 0, ctx->stream>>>(src, idx, n, out);
-  BGNN_LAUNCHED(ctx);
   return BGNN_OK;
 }
 

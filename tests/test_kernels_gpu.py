@@ -104,7 +104,7 @@ def test_out_of_range_edge_raises(bg):
 
 
 @pytest.mark.parametrize("nnz,m,ncol", [(0, 3, 3), (17, 5, 4), (100000, 3000, 5000),
-                                        (400000, 70000, 300)])
+                                        (400000, 70000, 300), (3000000, 1100000, 16000000)])
 def test_coo_to_csr_bit_exact(bg, torch, nnz, m, ncol):
     rng = np.random.default_rng(nnz + m)
     rows = rng.integers(0, m, nnz).astype(np.uint32)
@@ -119,6 +119,31 @@ def test_coo_to_csr_bit_exact(bg, torch, nnz, m, ncol):
     # and through the host facade
     rp, ci, va = bg.CudaComputeManager().coo_to_csr(rows, cols, vals, m, ncol)
     assert np.array_equal(rp, orp) and np.array_equal(ci, oci)
+
+
+def test_coo_to_csr_without_values(bg, torch):
+    """bgnn_coo_to_csr_dev with no input values (all ones, fromEdgeIndex) and
+    with no value output: the same rows and columns as the oracle."""
+    from browsergnn_b200.backend import ptr
+
+    rng = np.random.default_rng(11)
+    nnz, m, ncol = 250000, 4000, 70000
+    rows = rng.integers(0, m, nnz).astype(np.uint32)
+    cols = rng.integers(0, ncol, nnz).astype(np.uint32)
+    orp, oci, _ = orc.coo_to_csr(rows, cols, np.ones(nnz, np.float32), m)
+    ctx = bg.get_context()
+    r = torch.from_numpy(rows.view(np.int32)).cuda()
+    c = torch.from_numpy(cols.view(np.int32)).cuda()
+    for with_val_out in (True, False):
+        rp = torch.empty(m + 1, dtype=torch.int32, device="cuda")
+        ci = torch.empty(nnz, dtype=torch.int32, device="cuda")
+        va = torch.full((nnz,), -1.0, device="cuda") if with_val_out else None
+        ctx.call("bgnn_coo_to_csr_dev", ptr(r), ptr(c), None, nnz, m, ncol, ptr(rp), ptr(ci),
+                 ptr(va))
+        assert np.array_equal(rp.cpu().numpy().view(np.uint32), orp)
+        assert np.array_equal(ci.cpu().numpy().view(np.uint32), oci)
+        if with_val_out:
+            assert bool((va == 1.0).all())
 
 
 @pytest.mark.parametrize("loops", [False, True])
