@@ -60,18 +60,36 @@ def peaks():
 
 
 def profile_traffic(name):
-    """dram bytes per launch from a committed ncu summary (profiles/<name>.md,
-    a line 'dram_bytes_per_launch: <int>'), or None."""
+    """(dram bytes per launch, where the figure comes from) from a committed
+    ncu summary (profiles/<name>.md, lines 'dram_bytes_per_launch: <int>' and
+    'captured: <what>'), or (None, None)."""
     p = os.path.join(ROOT, "profiles", name + ".md")
     if not os.path.exists(p):
-        return None
+        return None, None
+    val, what = None, None
     for line in open(p):
-        if line.strip().startswith("dram_bytes_per_launch:"):
+        t = line.strip()
+        if t.startswith("dram_bytes_per_launch:"):
             try:
-                return int(line.split(":", 1)[1].strip().split()[0])
+                val = int(t.split(":", 1)[1].strip().split()[0])
             except ValueError:
-                return None
-    return None
+                val = None
+        elif t.startswith("captured:"):
+            what = t.split(":", 1)[1].strip()
+    src = f"profiles/{name}.md" + (f" ({what})" if what else "")
+    return val, src
+
+
+def max_over_ranks(v):
+    """Element-wise maximum over the ranks of a float or a list of floats."""
+    import torch
+    import torch.distributed as dist
+
+    scalar = not isinstance(v, (list, tuple))
+    t = torch.tensor([v] if scalar else list(v), dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    out = t.tolist()
+    return out[0] if scalar else out
 
 
 class ClockSampler:
@@ -153,10 +171,10 @@ def build_layers(weights, device):
     return layers
 
 
-def sage_forward(layers, dg, x, exchange=None, timers=None):
-    """Three SAGEConv layers (aggregate -> fused dual GEMM + bias + ReLU).
-    `exchange(x_local) -> x_ext` fills halo rows for a partitioned graph.
-    `timers` collects CUDA events around each phase (exchange, aggregate, linear)."""
+def sage_forward(layers, dg, x, timers=None):
+    """Three SAGEConv layers on one GPU (aggregate -> fused dual GEMM + bias +
+    ReLU).  `timers` collects CUDA events around each phase (aggregate,
+    linear)."""
     import torch
 
     from browsergnn_b200.backend import ptr
@@ -175,10 +193,9 @@ def sage_forward(layers, dg, x, exchange=None, timers=None):
     for li, lay in enumerate(layers):
         fin, fout = lay.inChannels, lay.outChannels
         e0 = mark()
-        src = exchange(h) if exchange is not None else h
         agg = torch.empty((n_own, fin), dtype=torch.float32, device=h.device)
         e1 = mark()
-        ctx.call("bgnn_aggregate", dg.h, 1, ptr(src), fin, ptr(agg))
+        ctx.call("bgnn_aggregate", dg.h, 1, ptr(h), fin, ptr(agg))
         e2 = mark()
         out = torch.empty((n_own, fout), dtype=torch.float32, device=h.device)
         act = 1 if li < len(layers) - 1 else 0  # ReLU between layers (wasmRelu)
@@ -192,151 +209,158 @@ def sage_forward(layers, dg, x, exchange=None, timers=None):
     return h
 
 
-class PartitionedSage:
-    """The same three layers on one rank of a row partition.  Buffers are
-    allocated once: per layer an [owned | halo] feature buffer whose owned
-    rows the previous layer writes directly, so the exchange only fills the
-    halo rows.  For outputs wider than 64 the self product x*W_self runs on a
-    side stream while the halo rows are in flight; the neighbour product then
-    adds to it (bgnn_linear_add), the same two f32 results and the same final
-    rounding as bgnn_sage_linear."""
+def dist_forward(layers, pgd, timers=None):
+    """The same three layers on one rank of the row partition
+    (browsergnn_b200.distributed): each SAGEConv.forward on the
+    PartitionedGraphData exchanges its input's halo rows with NCCL in column
+    chunks pipelined with the aggregation, runs x * W_self on a side stream,
+    and writes its output into the owned rows of the next layer's
+    [owned | halo] buffer.  `timers` collects CUDA events around each layer."""
+    import torch
 
-    def __init__(self, layers, part, dg, x, ctx, peer_stores=False):
-        import torch
+    h = pgd
+    for li, lay in enumerate(layers):
+        a = b = None
+        if timers is not None:
+            a = torch.cuda.Event(enable_timing=True)
+            a.record()
+        h = lay.forward(h, _act="relu" if li < len(layers) - 1 else None)
+        if timers is not None:
+            b = torch.cuda.Event(enable_timing=True)
+            b.record()
+            timers.append((li, lay.inChannels, None, None, a, b))
+    return h.x
 
-        from browsergnn_b200.partition import PeerStores, SharedBuffer
 
-        self.layers, self.part, self.dg, self.ctx = layers, part, dg, ctx
-        n_own, n_ext = part.n_own, part.n_own + part.n_halo
-        dev = x.device
-        # Layers 2.. read buffers that the previous layer's epilogue fills,
-        # halo rows included, by storing into the peers' mapped buffers
-        # (bgnn_linear_add_remote); the input features go through the
-        # all-to-all.
-        self.shared = []
-        self.peer = None
-        self.ext = [torch.empty((n_ext, layers[0].inChannels), dtype=torch.float32, device=dev)]
-        for lay in layers[1:]:
-            if peer_stores:
-                b = SharedBuffer(ctx, n_ext, lay.inChannels)
-                self.shared.append(b)
-                self.ext.append(b.tensor)
-            else:
-                self.ext.append(torch.empty((n_ext, lay.inChannels), dtype=torch.float32,
-                                            device=dev))
-        if peer_stores:
-            self.peer = PeerStores(part, ctx, self.shared)
-        self.flag = torch.zeros(1, dtype=torch.float32, device=dev)
-        self.ext[0][:n_own].copy_(x)
-        self.agg = [torch.empty((n_own, lay.inChannels), dtype=torch.float32, device=dev)
-                    for lay in layers]
-        self.st = [torch.empty((n_own, lay.outChannels), dtype=torch.float32, device=dev)
-                   for lay in layers]
-        self.out = torch.empty((n_own, layers[-1].outChannels), dtype=torch.float32, device=dev)
-        self.send = [torch.empty((part.n_send, lay.inChannels), dtype=torch.float32, device=dev)
-                     for lay in layers]
-        self.side = torch.cuda.Stream(device=dev)
-        from browsergnn_b200.partition import cuda_pack
+def exchange_times(pg, dctx, reps):
+    """The halo exchange alone (bgnn_dist_exchange, whole width in one NCCL
+    group) per layer input width: ms, mean over reps, max over ranks."""
+    import torch
+    import torch.distributed as dist
 
-        self.pack = cuda_pack(ctx)
+    from browsergnn_b200.backend import ptr
 
-    def close(self):
-        """Unmap the peers' buffers everywhere, then free this rank's."""
-        import torch.distributed as dist
-
-        import torch
-
+    res = {}
+    for f in sorted(set(WIDTHS[:-1])):
+        ext = pg.ext_buffer(f)
+        ext.normal_()
+        for _ in range(2):
+            pg.ctx.call_on("bgnn_dist_exchange", dctx.h, pg.h, ptr(ext), f)
         torch.cuda.synchronize()
-        if self.peer is not None:
-            self.peer.close()
-        dist.barrier(group=self.part.group)
-        for b in self.shared:
-            b.free()
-        self.shared = []
+        dist.barrier()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            pg.ctx.call_on("bgnn_dist_exchange", dctx.h, pg.h, ptr(ext), f)
+        b.record()
+        dctx.synchronize()
+        ms = max_over_ranks(a.elapsed_time(b) / reps)
+        recv = max_over_ranks(float(pg.n_halo * f * 4))
+        res[f"F{f}"] = {"ms": round(ms, 3), "max_recv_bytes": int(recv),
+                        "recv_GBps_at_max": round(recv / (ms * 1e-3) / 1e9, 1)}
+        del ext
+    return res
 
-    def forward(self, timers=None):
-        import torch
-        import torch.distributed as dist
 
-        from browsergnn_b200.backend import ptr
+def e2e_single(layers, ei, x, n, e, warmup, steps):
+    """The public API from pinned host buffers: GraphData from the step's
+    host edge list and features (the edge list uploaded and the CSR built and
+    validated on the device while the features upload on a copy stream), 3
+    layers, the result read back."""
+    import torch
 
-        ctx, part, dg = self.ctx, self.part, self.dg
-        n_own = part.n_own
-        main = torch.cuda.current_stream()
+    import browsergnn_b200 as bg
 
-        def mark():
-            if timers is None:
-                return None
-            ev = torch.cuda.Event(enable_timing=True)
-            ev.record()
-            return ev
+    ei_host = ei.cpu().pin_memory()
+    x_host = x.cpu().pin_memory()
+    res = torch.empty((n, WIDTHS[-1]), dtype=torch.float32, pin_memory=True)
+    times = []
+    for i in range(warmup + steps):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        g = bg.GraphData(x=x_host, numNodes=n, numFeatures=WIDTHS[0], edgeIndex=ei_host,
+                         numEdges=e)
+        out = g
+        for li, lay in enumerate(layers):
+            out = lay.forward(out, _act="relu" if li < 2 else None)
+        res.copy_(out.x)
+        t1 = time.perf_counter()
+        out.device_graph().close()
+        if i >= warmup:
+            times.append(t1 - t0)
+    s = statistics.mean(times)
+    return {"value": 3 * e / s, "unit": UNIT,
+            "h2d_bytes_per_step": int(x_host.numel() * 4 + ei_host.numel() * 4),
+            "d2h_bytes_per_step": int(res.numel() * 4), "ms_per_step": round(1000 * s, 3),
+            "includes": "H2D of features and edge index (pinned), device CSR build, 3 layers, "
+                        "D2H of the result"}
 
-        nl = len(self.layers)
-        remote_done = [False] * nl  # layer li stored its rows into the peers' halos
-        for li, lay in enumerate(self.layers):
-            fin, fout = lay.inChannels, lay.outChannels
-            ext, agg = self.ext[li], self.agg[li]
-            out = self.ext[li + 1][:n_own] if li + 1 < nl else self.out
-            act = 1 if li < nl - 1 else 0
-            split = fout > 64
-            # halo rows already filled by the previous layer's epilogue (only
-            # when that layer ran the split, remote-storing linear)
-            halo_ready = li > 0 and remote_done[li - 1]
-            remote_out = self.peer is not None and li + 1 < nl and split
-            e0 = mark()
-            # pack the rows the other ranks need, then start x * W_self (owned
-            # rows only) on the side stream while the rows are exchanged
-            if not halo_ready:
-                part.pack_send(ext, self.pack, self.send[li])
-            if split:
-                self.side.wait_stream(main)
-                with torch.cuda.stream(self.side):
-                    ctx.call("bgnn_linear", ptr(ext), ptr(lay.p("lin_self")), n_own, fin, fout,
-                             None, 0, 0.0, ptr(self.st[li]))
-            if not halo_ready:
-                part.send_recv(ext, self.send[li])
-            e1 = mark()
-            ctx.call("bgnn_aggregate", dg.h, 1, ptr(ext), fin, ptr(agg))
-            e2 = mark()
-            if remote_out:
-                # the next layer's input: own rows here, halo rows in the peers
-                main.wait_stream(self.side)
-                pr = self.peer
-                ctx.call("bgnn_linear_add_remote", ptr(agg), ptr(lay.p("lin_neighbor")), n_own,
-                         fin, fout, ptr(self.st[li]), ptr(lay.p("bias")), act, 0.0, ptr(out),
-                         ptr(pr.row_ptr), ptr(pr.dst), ptr(pr.tables[li]), ptr(pr.peer_rows),
-                         part.world)
-                # every rank's stores land before anyone reads its halo rows
-                dist.all_reduce(self.flag, group=part.group)
-                remote_done[li] = True
-            elif split:
-                main.wait_stream(self.side)
-                ctx.call("bgnn_linear_add", ptr(agg), ptr(lay.p("lin_neighbor")), n_own, fin,
-                         fout, ptr(self.st[li]), ptr(lay.p("bias")), act, 0.0, ptr(out))
-            else:
-                ctx.call("bgnn_sage_linear", ptr(agg), ptr(ext), ptr(lay.p("lin_neighbor")),
-                         ptr(lay.p("lin_self")), n_own, fin, fout, ptr(lay.p("bias")), act,
-                         0.0, ptr(out))
-            e3 = mark()
-            if timers is not None:
-                timers.append((li, fin, e1, e2, e0, e3))
-        return self.out
+
+def e2e_partitioned(layers, ei, x_own, pg0, n, e, dctx, rank, world, warmup, steps):
+    """The public API on every rank from pinned host buffers: the full edge
+    list in (each rank derives the partition plan from it on its device: CSR
+    build, bounds, halo and send lists), this rank's feature rows in, 3
+    partitioned layers, this rank's output rows out.  Host wall time per
+    step, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from browsergnn_b200 import distributed
+
+    ei_host = ei.cpu().pin_memory()
+    # every rank holds the whole feature matrix on the host, as a user would
+    x_host = torch.empty((n, WIDTHS[0]), dtype=torch.float32, pin_memory=True)
+    x_host[pg0.lo:pg0.hi].copy_(x_own)
+    res = torch.empty((pg0.n_own, WIDTHS[-1]), dtype=torch.float32, pin_memory=True)
+    times = []
+    h2d = d2h = 0
+    for i in range(warmup + steps):
+        dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        pg = distributed.PartitionedGraph.from_edge_index(ei_host, e, n, world, rank)
+        ext = pg.ext_buffer(WIDTHS[0])
+        ext[: pg.n_own].copy_(x_host[pg.lo:pg.hi], non_blocking=True)
+        h = distributed.PartitionedGraphData(pg, dctx, ext, WIDTHS[0])
+        for li, lay in enumerate(layers):
+            h = lay.forward(h, _act="relu" if li < 2 else None)
+        res[: pg.n_own].copy_(h.x)
+        t1 = time.perf_counter()
+        h2d = ei_host.numel() * 4 + pg.n_own * WIDTHS[0] * 4
+        d2h = pg.n_own * WIDTHS[-1] * 4
+        h = None
+        pg.close()
+        if i >= warmup:
+            times.append(t1 - t0)
+    s = max_over_ranks(statistics.mean(times))
+    return {"value": 3 * e / s, "unit": UNIT, "h2d_bytes_per_step": int(max_over_ranks(h2d)),
+            "d2h_bytes_per_step": int(max_over_ranks(d2h)), "ms_per_step": round(1000 * s, 3),
+            "includes": "per rank: H2D of the full edge list and the rank's feature rows "
+                        "(pinned), device CSR build and partition plan, 3 layers with NCCL halo "
+                        "exchange, D2H of the rank's rows; host wall time, max over ranks"}
 
 
 # ---------------------------------------------------------------------------
 # SpMM sweep (standalone CSR SpMM, scale-24 R-MAT, 2^28 edges)
 # ---------------------------------------------------------------------------
-def spmm_sweep(steps, warmup, hbm_peak, parity=True):
+def spmm_sweep(steps, warmup, hbm_peak, parity=True, dctx=None, rank=0, world=1):
+    """The standalone CSR SpMM (SparseCSR.matmul) of the scale-24 R-MAT
+    matrix with 2^28 entries at F = 32/64/128/256.  N>1: rows partitioned
+    across the ranks (browsergnn_b200.distributed.PartitionedGraph.from_csr),
+    the halo rows of X exchanged with NCCL in column chunks pipelined with
+    the local SpMM; time = max over ranks."""
     import torch
 
     import browsergnn_b200 as bg
     from browsergnn_b200 import synth
     from browsergnn_b200.backend import ptr
 
+    dev = torch.cuda.current_device()
     n, e, scale = 1 << synth.SPMM_SCALE, synth.SPMM_E, synth.SPMM_SCALE
     seed = synth.seed_for(5)
-    ei = synth.rmat_edges_gpu(scale, n, e, seed)
-    ctx = bg.get_context()
+    ei = synth.rmat_edges_gpu(scale, n, e, seed, device=dev)
+    ctx = bg.get_context(dev)
     # values f32(u * dinv[src] * dinv[dst]) with u ~ U(0,1] and dinv from the in-degree
     dinv = bg.compute_gcn_norm(ei, e, n, False)  # dinv[s]*dinv[t] per edge
     u = 1.0 - torch.rand(e, device="cuda", generator=torch.Generator("cuda").manual_seed(seed))
@@ -344,49 +368,93 @@ def spmm_sweep(steps, warmup, hbm_peak, parity=True):
     del dinv
     rows = ei[:e]
     cols = ei[e:]
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    t0.record()
-    csr = bg.SparseCSR.fromCOO(bg.SparseCOO(rows, cols, vals, (n, n)))
-    t1.record()
-    torch.cuda.synchronize()
-    build_ms = t0.elapsed_time(t1)
-    del ei, rows, cols, vals, u
+    coo = bg.SparseCOO(rows, cols, vals, (n, n), device=dev)
+    for rep in range(2):  # the first build also grows the memory pool
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        csr = bg.SparseCSR.fromCOO(coo)
+        t1.record()
+        torch.cuda.synchronize()
+        build_ms = t0.elapsed_time(t1)
+        if rep == 0:
+            first_ms = build_ms
+            del csr
+    del ei, rows, cols, vals, u, coo
     g = csr.graph()
-    res = {"workload": f"spmm-rmat-s{scale}-{n}n-{e}e", "csr_build_ms": round(build_ms, 3)}
+    res = {"workload": f"spmm-rmat-s{scale}-{n}n-{e}e", "csr_build_ms": round(build_ms, 3),
+           "csr_build_first_ms": round(first_ms, 3),
+           "csr_build": "SparseCSR.fromCOO of 2^28 entries on the device (stable (row, col) "
+                        "radix sort), second call; the first also grows the memory pool"}
+    pg = None
+    if world > 1:
+        from browsergnn_b200 import distributed
+
+        t0 = time.perf_counter()
+        pg = distributed.PartitionedGraph.from_csr(csr, world, rank)
+        torch.cuda.synchronize()
+        res["partition_plan_s"] = round(max_over_ranks(time.perf_counter() - t0), 3)
+        res["parallelism"] = f"row-partition x{world}"
+        res["scaling"] = "strong"
     per_f = {}
     gen = torch.Generator("cuda").manual_seed(seed + 1)
     host_csr = None
-    if parity:
+    if parity and world == 1:
         host_csr = (csr.rowPtr.cpu().numpy().view(np.uint32),
                     csr.colIndices.cpu().numpy().view(np.uint32), csr.values.cpu().numpy())
     for f in (32, 64, 128, 256):
         x = torch.randn((n, f), device="cuda", generator=gen)
-        out = torch.empty((n, f), device="cuda")
+        if pg is None:
+            out = torch.empty((n, f), device="cuda")
+
+            def run():
+                ctx.call("bgnn_graph_spmm", g.h, ptr(csr.values), ptr(x), f, ptr(out))
+        else:
+            ext = pg.ext_buffer(f)
+            ext[: pg.n_own].copy_(x[pg.lo:pg.hi])
+            out = torch.empty((pg.n_own, f), device="cuda")
+
+            def run():
+                pg.spmm(dctx, csr.values, ext, out)
         for _ in range(warmup):
-            ctx.call("bgnn_graph_spmm", g.h, ptr(csr.values), ptr(x), f, ptr(out))
+            run()
         torch.cuda.synchronize()
-        evs = []
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
         for _ in range(steps):
-            a = torch.cuda.Event(enable_timing=True)
-            b = torch.cuda.Event(enable_timing=True)
-            a.record()
-            ctx.call("bgnn_graph_spmm", g.h, ptr(csr.values), ptr(x), f, ptr(out))
-            b.record()
-            evs.append((a, b))
+            run()
+        b.record()
         torch.cuda.synchronize()
-        ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+        ms = a.elapsed_time(b) / steps
+        if world > 1:
+            ms = max_over_ranks(ms)
         bytes_alg = 4 * (n + 1) + 8 * e + 4 * f * e + 4 * f * n  # rowPtr, col, val, gathers, out
         gbs = bytes_alg / (ms * 1e-3) / 1e9
         per_f[str(f)] = {"ms": round(ms, 3), "edges_per_s": e / (ms * 1e-3),
                          "gather_model_GBps": round(gbs, 1),
-                         "hbm_frac_gather_model": round(gbs / hbm_peak, 3),
+                         "hbm_frac_gather_model": round(gbs / hbm_peak / world, 3),
                          "compulsory_GBps": round((4 * (n + 1) + 8 * e + 8 * f * n)
                                                   / (ms * 1e-3) / 1e9, 1)}
         if host_csr is not None and f in (32, 256):
             per_f[str(f)]["parity"] = spmm_parity(host_csr, x, out, f, seed)
+        if pg is not None and parity and f in (32, 256):
+            # each rank's rows against a single-GPU SpMM of the whole matrix
+            full = torch.empty((n, f), device="cuda")
+            ctx.call("bgnn_graph_spmm", g.h, ptr(csr.values), ptr(x), f, ptr(full))
+            mine = full[pg.lo:pg.hi]
+            bad = int((mine.view(torch.int32) != out.view(torch.int32)).sum().item())
+            tot = max_over_ranks([float(bad)])
+            per_f[str(f)]["bit_identical_to_1gpu"] = tot[0] == 0
+            del full, mine
         del x, out
     res["per_feature_width"] = per_f
+    if pg is not None:
+        pg.close()
     g.close()
     return res
 
@@ -404,7 +472,7 @@ def partition_bit_identity(ei, n, e, seed, layers, part, got, device):
     gen = torch.Generator("cuda").manual_seed(seed)
     x_full = torch.randn((n, WIDTHS[0]), device="cuda", generator=gen)
     dg = DeviceGraph(ei, e, n, n, device=device)
-    ref = sage_forward(layers, dg, x_full, None, None)
+    ref = sage_forward(layers, dg, x_full)
     mine = ref[part.lo:part.hi]
     bad = (mine.view(torch.int32) != got.view(torch.int32)) & ~(torch.isnan(mine) & torch.isnan(got))
     counts = torch.tensor([int(bad.sum().item()), int(got.numel())], device="cuda",
@@ -761,10 +829,10 @@ def main():
     ap.add_argument("--no-small", action="store_true")
     ap.add_argument("--no-parity", action="store_true",
                     help="skip the full-size output checks (oracle at N=1, N=1 bits at N>1)")
-    ap.add_argument("--peer-stores", action="store_true",
-                    help="N>1: layers 2-3 get their halo rows from the previous layer's epilogue "
-                         "storing into the peers' buffers instead of the all-to-all (bit-identical; "
-                         "faster at 2 GPUs, slower at 8: 16-byte peer stores use NVLink poorly)")
+    ap.add_argument("--chunks", type=int, default=None,
+                    help="N>1: column chunks of the pipelined halo exchange (0: by width)")
+    ap.add_argument("--reserve-sms", type=int, default=16,
+                    help="N>1: SMs the aggregation leaves to NCCL while chunks are in flight")
     ap.add_argument("--profile", choices=["small", "full-agg", "csr"], default=None,
                     help="run one profiling case for ncu and exit")
     args = ap.parse_args()
@@ -812,23 +880,31 @@ def main():
     layers = build_layers(weights, local)
 
     t0 = time.perf_counter()
+    dctx = pgd = None
     if world > 1:
-        from browsergnn_b200.partition import HaloPlan
+        from browsergnn_b200 import distributed
 
-        part = HaloPlan(ei[:e], ei[e:], n, rank, world)
-        dg = part.device_graph(local)
-        x = x_full[part.lo:part.hi].contiguous()
-        psage = PartitionedSage(layers, part, dg, x, ctx, peer_stores=args.peer_stores)
-        step = psage.forward
+        distributed.nccl_env_defaults()
+        dctx = distributed.DistContext(rank, world, device=local, timeout_ms=120_000)
+        if args.chunks is not None:
+            dctx.set_pipeline(args.chunks, args.reserve_sms)
+        pg = distributed.PartitionedGraph.from_edge_index(ei, e, n, world, rank, device=local)
+        ext0 = pg.ext_buffer(WIDTHS[0])
+        ext0[: pg.n_own].copy_(x_full[pg.lo:pg.hi])
+        pgd = distributed.PartitionedGraphData(pg, dctx, ext0, WIDTHS[0])
+        x = ext0[: pg.n_own]
+        dg = None
+        step = lambda timers=None: dist_forward(layers, pgd, timers)  # noqa: E731
     else:
         from browsergnn_b200.graph import DeviceGraph
 
         dg = DeviceGraph(ei, e, n, n, device=local)
         x = x_full
-        part = None
-        step = lambda timers=None: sage_forward(layers, dg, x, None, timers)  # noqa: E731
+        step = lambda timers=None: sage_forward(layers, dg, x, timers)  # noqa: E731
     torch.cuda.synchronize()
     build_s = time.perf_counter() - t0
+    if world > 1:
+        build_s = max_over_ranks(build_s)
     del x_full
 
     def barrier():
@@ -857,82 +933,65 @@ def main():
     torch.cuda.synchronize()
     ms_total = start.elapsed_time(stop)
     if world > 1:
-        t = torch.tensor([ms_total], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_total = float(t.item())
+        ms_total = max_over_ranks(ms_total)
     ms_step = ms_total / args.steps
     value = 3 * e / (ms_step * 1e-3)  # whole-job: all ranks' edges / max time
 
-    # roofline of the dominant kernel: the F=256 aggregation (layers 2 and 3)
+    # per-layer phases (mean over steps, max over ranks)
     agg_ms = {}
-    phases = {}  # per layer: exchange, aggregate, linear (ms, mean over steps)
+    phases = {}
     for li, fin, a, b, x0, l1 in timers:
-        agg_ms.setdefault((li, fin), []).append(a.elapsed_time(b))
-        ph = phases.setdefault(li, [[], [], []])
-        ph[0].append(x0.elapsed_time(a))
-        ph[1].append(a.elapsed_time(b))
-        ph[2].append(b.elapsed_time(l1))
-    phase_vec = [statistics.mean(v) for li in sorted(phases) for v in phases[li]]
+        ph = phases.setdefault(li, {})
+        if a is not None:
+            agg_ms.setdefault((li, fin), []).append(a.elapsed_time(b))
+            ph.setdefault("aggregate", []).append(a.elapsed_time(b))
+            ph.setdefault("linear", []).append(b.elapsed_time(l1))
+        ph.setdefault("layer", []).append(x0.elapsed_time(l1))
+    keys = [(li, k) for li in sorted(phases) for k in sorted(phases[li])]
+    vec = [statistics.mean(phases[li][k]) for li, k in keys]
     if world > 1:
-        pv = torch.tensor(phase_vec, device="cuda", dtype=torch.float64)
-        dist.all_reduce(pv, op=dist.ReduceOp.MAX)
-        phase_vec = pv.tolist()
-    phase_ms = {f"L{li + 1}": {"exchange": round(phase_vec[3 * i], 3),
-                               "aggregate": round(phase_vec[3 * i + 1], 3),
-                               "linear": round(phase_vec[3 * i + 2], 3)}
-                for i, li in enumerate(sorted(phases))}
-    n_dst = dg.num_dst
-    e_loc = dg.num_edges
-    f = 256
-    bytes_alg = 4 * (n_dst + 1) + 4 * e_loc + 4 * f * e_loc + 4 * f * n_dst
-    t256 = [m for (li, fin), v in agg_ms.items() if fin == 256 for m in v]
-    agg_avg_ms = statistics.mean(t256)
-    achieved = bytes_alg / (agg_avg_ms * 1e-3) / 1e9
-    traffic = profile_traffic("aggregate_mean_f256_sage_rmat") if world == 1 else None
-    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak,
-                "unit": "GB/s", "frac": round(achieved / hbm_peak, 3), "traffic": traffic,
-                "kernel": "aggregate mean F=256 (streaming kernel, one launch)",
-                # the gather model gives no credit for L2 hits, which R-MAT hubs
-                # get: the DRAM bytes ncu counts (traffic) over the same time
-                "dram_achieved": (round(traffic / (agg_avg_ms * 1e-3) / 1e9, 1)
+        vec = max_over_ranks(vec)
+    phase_ms = {}
+    for (li, k), v in zip(keys, vec):
+        phase_ms.setdefault(f"L{li + 1}", {})[k] = round(v, 3)
+
+    roofline = None
+    if world == 1:
+        # the dominant kernel: the F=256 aggregation (layers 2 and 3)
+        f = 256
+        bytes_alg = 4 * (n + 1) + 4 * e + 4 * f * e + 4 * f * n
+        agg_avg_ms = statistics.mean([m for (li, fin), v in agg_ms.items() if fin == 256
+                                      for m in v])
+        achieved = bytes_alg / (agg_avg_ms * 1e-3) / 1e9
+        traffic, tsrc = profile_traffic("aggregate_mean_f256_sage_rmat")
+        roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak,
+                    "unit": "GB/s", "frac": round(achieved / hbm_peak, 3), "traffic": traffic,
+                    "traffic_source": tsrc,
+                    "kernel": "aggregate mean F=256 (streaming kernel, one launch)",
+                    # the gather model gives no credit for L2 hits, which R-MAT
+                    # hubs get: the DRAM bytes ncu counts over the same time
+                    "dram_achieved": (round(traffic / (agg_avg_ms * 1e-3) / 1e9, 1)
+                                      if traffic else None),
+                    "dram_frac": (round(traffic / (agg_avg_ms * 1e-3) / 1e9 / hbm_peak, 3)
                                   if traffic else None),
-                "dram_frac": (round(traffic / (agg_avg_ms * 1e-3) / 1e9 / hbm_peak, 3)
-                              if traffic else None),
-                "bytes_model": "gather model: 4(N+1) + 4E + 4FE + 4FN",
-                "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
-                "launch_ms": round(agg_avg_ms, 3),
-                "per_layer_aggregate_ms": {f"L{li + 1}_F{fin}": round(statistics.mean(v), 3)
-                                           for (li, fin), v in sorted(agg_ms.items())}}
+                    "bytes_model": "gather model: 4(N+1) + 4E + 4FE + 4FN",
+                    "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
+                    "launch_ms": round(agg_avg_ms, 3),
+                    "per_layer_aggregate_ms": {f"L{li + 1}_F{fin}": round(statistics.mean(v), 3)
+                                               for (li, fin), v in sorted(agg_ms.items())}}
+
+    exchange_only = None
+    if world > 1:
+        exchange_only = exchange_times(pgd.pg, dctx, max(3, args.steps // 2))
 
     # e2e through the public API: host features + host edge index each step
     e2e = None
-    if not args.no_e2e and world == 1:
-        ei_host = ei.cpu().pin_memory()
-        x_host = x.cpu().pin_memory()
-        res = torch.empty((n, WIDTHS[-1]), dtype=torch.float32, pin_memory=True)
-        e2e_times = []
-        for i in range(args.warmup + args.steps):
-            torch.cuda.synchronize()
-            t0 = time.perf_counter()
-            # the user's call: GraphData from the step's pinned host edge list
-            # and features (edges uploaded and the CSR built and validated on
-            # the device while the features upload on a copy stream), 3
-            # layers, read the result back
-            g = bg.GraphData(x=x_host, numNodes=n, numFeatures=WIDTHS[0], edgeIndex=ei_host,
-                             numEdges=e)
-            out = g
-            for li, lay in enumerate(layers):
-                out = lay.forward(out, _act="relu" if li < 2 else None)
-            res.copy_(out.x)
-            t1 = time.perf_counter()
-            out.device_graph().close()
-            if i >= args.warmup:
-                e2e_times.append(t1 - t0)
-        e2e_s = statistics.mean(e2e_times)
-        e2e = {"value": 3 * e / e2e_s, "unit": UNIT,
-               "h2d_bytes_per_step": int(x_host.numel() * 4 + ei_host.numel() * 4),
-               "d2h_bytes_per_step": int(res.numel() * 4), "ms_per_step": round(1000 * e2e_s, 3),
-               "includes": "H2D of features and edge index, device CSR build, 3 layers, D2H"}
+    if not args.no_e2e:
+        if world == 1:
+            e2e = e2e_single(layers, ei, x, n, e, args.warmup, args.steps)
+        else:
+            e2e = e2e_partitioned(layers, ei, x, pgd.pg, n, e, dctx, rank, world,
+                                  args.warmup, args.steps)
 
     # parity at full size: N=1 against the oracle (every output element);
     # N>1 bit for bit against a single-GPU forward of the whole graph, which
@@ -942,7 +1001,7 @@ def main():
         if world == 1:
             parity = sage_oracle_parity(ei, n, e, x, weights, final)
         else:
-            parity = partition_bit_identity(ei, n, e, seed, layers, part, final, local)
+            parity = partition_bit_identity(ei, n, e, seed, layers, pgd.pg, final, local)
     del final
 
     cpu = None
@@ -952,11 +1011,24 @@ def main():
         cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
                "sample": desc + " (best of 3)"}
 
+    part_info = None
+    if world > 1:
+        pg = pgd.pg
+        part_info = {"rows": pg.n_own, "halo_rows": pg.n_halo, "send_rows": pg.n_send,
+                     "local_edges": pg.num_local_edges}
+        allinfo = [None] * world
+        dist.all_gather_object(allinfo, part_info)
+        part_info = {"per_rank": allinfo,
+                     "halo_exchange": "NCCL grouped send/recv in column chunks, pipelined "
+                                      "with the aggregation (browsergnn_b200.distributed)"}
+        pgd = None
+        pg.close()
     spmm = None
-    if not args.no_spmm and world == 1:
+    if not args.no_spmm:
         del dg
         torch.cuda.empty_cache()
-        spmm = spmm_sweep(max(3, args.steps // 2), 3, hbm_peak, parity=not args.no_parity)
+        spmm = spmm_sweep(max(3, args.steps // 2), 3, hbm_peak, parity=not args.no_parity,
+                          dctx=dctx, rank=rank, world=world)
     small = None
     if not args.no_small and world == 1:
         small = small_workloads(max(3, args.steps), 3)
@@ -977,19 +1049,17 @@ def main():
             "phase_ms_max_over_ranks": phase_ms,
             "parity": parity,
         }
-        if part is not None:
-            line["config"]["halo_rows_rank0"] = part.n_halo
-            line["config"]["halo_exchange"] = (
-                "layer 1: NCCL all-to-all; layers 2-3: peer stores from the previous layer's "
-                "epilogue + one barrier" if psage.peer is not None else "NCCL all-to-all")
+        if part_info is not None:
+            line["partition"] = part_info
+            line["exchange_only_ms_max_over_ranks"] = exchange_only
         if spmm is not None:
             line["spmm_sweep"] = spmm
         if small is not None:
             line["workloads"] = small
         print(json.dumps(line), flush=True)
     if world > 1:
-        psage.close()
         dist.barrier()
+        dctx.close()
         dist.destroy_process_group()
 
 

@@ -17,6 +17,7 @@ OK, ERR_INVALID_ARG, ERR_OUT_OF_RANGE, ERR_CUDA, ERR_NO_MEMORY, ERR_TIMEOUT, ERR
     ERR_DEVICE = range(8)
 MATH_FAST, MATH_EXACT = 0, 1
 AGGR = {"sum": 0, "add": 0, "mean": 1, "max": 2}
+AGGR_SPMM = 3
 ACT = {None: 0, "none": 0, "relu": 1, "relu_max": 2, "elu": 3, "leaky_relu": 4, "sigmoid": 5,
        "tanh": 6, "gelu": 7, "silu": 8}
 LINK = {"dot": 0, "bilinear": 1, "mlp": 2}
@@ -93,13 +94,6 @@ SIGNATURES = {
     "bgnn_linear": [_P, _P, _P, _U32, _U32, _U32, _P, _I, _D, _P],
     "bgnn_sage_linear": [_P, _P, _P, _P, _P, _U32, _U32, _U32, _P, _I, _D, _P],
     "bgnn_linear_add": [_P, _P, _P, _U32, _U32, _U32, _P, _P, _I, _D, _P],
-    "bgnn_linear_add_remote": [_P, _P, _P, _U32, _U32, _U32, _P, _P, _I, _D, _P, _P, _P, _P, _P,
-                               _U32],
-    "bgnn_shared_alloc": [_P, _U64, ctypes.POINTER(_P)],
-    "bgnn_shared_free": [_P, _P],
-    "bgnn_ipc_handle": [_P, _P, _P],
-    "bgnn_ipc_open": [_P, _P, ctypes.POINTER(_P)],
-    "bgnn_ipc_close": [_P, _P],
     "bgnn_l2_normalize_rows": [_P, _P, _U32, _U32],
     "bgnn_sum_pool": [_P, _P, _U32, _U32, _P, _U32, _P],
     "bgnn_pack_rows": [_P, _P, _U32, _P, _U32, _U32, _P],
@@ -111,6 +105,29 @@ SIGNATURES = {
     "bgnn_dropout": [_P, _P, _U64, _D, _U64, _P],
     "bgnn_prelu": [_P, _P, _U64, _P, _U32, _P],
     "bgnn_link_scores": [_P, _P, _U32, _U32, _P, _P, _U64, _I, _P, _P, _P, _P, _P, _P],
+    "bgnn_aggregate_strided": [_P, _P, _I, _P, _P, _U64, _U32, _P, _U64],
+    "bgnn_part_create": [_P, _P, _U64, _U32, _U32, _U32, _I, ctypes.POINTER(_P)],
+    "bgnn_part_create_csr": [_P, _P, _P, _U32, _U32, _U32, ctypes.POINTER(_P)],
+    "bgnn_part_destroy": [_P],
+    "bgnn_part_info": [_P, ctypes.POINTER(_U32), ctypes.POINTER(_U32), ctypes.POINTER(_U32),
+                       ctypes.POINTER(_U64), ctypes.POINTER(_U64), ctypes.POINTER(_U64)],
+    "bgnn_part_bounds": [_P, ctypes.POINTER(_U32)],
+    "bgnn_part_counts": [_P, ctypes.POINTER(_U64), ctypes.POINTER(_U64)],
+    "bgnn_part_graph": [_P, ctypes.POINTER(_P)],
+    "bgnn_part_lists": [_P, _P, _P, _P],
+    "bgnn_part_pack": [_P, _P, _P, _U64, _U32, _U32, _P],
+    "bgnn_part_unpack": [_P, _P, _P, _U32, _P, _U64, _U32],
+    "bgnn_dist_unique_id": [_P],
+    "bgnn_dist_create": [_P, _P, _U32, _U32, _U32, _U32, ctypes.POINTER(_P)],
+    "bgnn_dist_destroy": [_P],
+    "bgnn_dist_abort": [_P],
+    "bgnn_dist_set_pipeline": [_P, _U32, _U32],
+    "bgnn_dist_exchange": [_P, _P, _P, _U32],
+    "bgnn_dist_aggregate": [_P, _P, _I, _P, _U32, _P],
+    "bgnn_dist_spmm": [_P, _P, _P, _P, _U32, _P],
+    "bgnn_dist_sage_layer": [_P, _P, _I, _P, _U32, _U32, _P, _P, _P, _I, _D, _P, _P],
+    "bgnn_dist_allreduce_max": [_P, ctypes.POINTER(_D), _U32],
+    "bgnn_dist_synchronize": [_P],
 }
 _RESTYPE = {"bgnn_last_error": ctypes.c_char_p, "bgnn_ctx_launch_count": ctypes.c_uint64}
 

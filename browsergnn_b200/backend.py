@@ -55,6 +55,13 @@ class CudaContext:
         rc = getattr(self.lib, name)(h, *args)
         _lib.check(rc, self.h)
 
+    def call_on(self, name: str, *args):
+        """Call an entry point whose first argument is another handle (a
+        partition, a communicator) that reports errors on this context."""
+        self.bind()
+        rc = getattr(self.lib, name)(*args)
+        _lib.check(rc, self.h)
+
     def set_math(self, exact: bool):
         mode = _lib.MATH_EXACT if exact else _lib.MATH_FAST
         _lib.check(self.lib.bgnn_ctx_set_math(self.h, mode), self.h)

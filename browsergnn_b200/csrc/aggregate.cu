@@ -689,7 +689,8 @@ int launch_stream_t(bgnn_ctx* ctx, const AggArgs& a, int P, int swp, int n_slice
                                                                ST_THREADS, smem));
   if (per_sm < 1) per_sm = 1;
   const uint64_t work = (uint64_t)a.n_items * n_slices;
-  uint64_t grid = (uint64_t)ctx->num_sms * per_sm;
+  const int sms = ctx->grid_sms > 0 && ctx->grid_sms < ctx->num_sms ? ctx->grid_sms : ctx->num_sms;
+  uint64_t grid = (uint64_t)sms * per_sm;
   if (grid > work) grid = work ? work : 1;
   // Giant rows: a heavy row whose bytes exceed one pipe's fair share of the
   // launch would finish long after the rest, so it is cut into feature slices
@@ -722,7 +723,7 @@ int launch_stream_t(bgnn_ctx* ctx, const AggArgs& a, int P, int swp, int n_slice
   if (n_giant > 0) {
     const double share = (double)a.num_edges * (double)F * 4.0 / (double)grid;
     const uint32_t gs = (uint32_t)((F + gsw - 1) / gsw);
-    const uint32_t cap = (uint32_t)ctx->num_sms / 4 / gs;
+    const uint32_t cap = (uint32_t)sms / 4 / gs;
     while (n_ex < n_giant && n_ex < cap && (double)a.heavy_deg[n_ex] * F * 4.0 > 4.0 * share) n_ex++;
   }
   int mode = 0;

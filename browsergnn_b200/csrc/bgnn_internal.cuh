@@ -25,6 +25,8 @@ struct bgnn_ctx {
   int math = BGNN_MATH_FAST;
   int* d_err = nullptr;      // [0]=code, [1]=info lo, [2]=info hi, [3]=where
   uint32_t* d_small = nullptr;  // small device counters (heavy-row count etc.)
+  int grid_sms = 0;  // SMs the persistent aggregation may fill (0: all); the multi-GPU
+                     // pipeline leaves the rest to the collectives running beside it
   uint64_t launches = 0;
   std::string last_error;
 };
@@ -51,6 +53,30 @@ struct bgnn_graph {
   float* dinv[2] = {nullptr, nullptr};  // GCN D^-1/2 without / with loop tail
   uint32_t* dst_of = nullptr;      // [E] destination row of each CSR slot (built on first use)
 };
+
+// Row partition of a square graph / CSR for one rank (partition.cu): rank r
+// owns rows [lo, hi); its local CSR holds those rows' entries in the global
+// order with columns relabelled to [0, n_own) for owned nodes and
+// n_own + k for the k-th halo node (sorted global id, hence grouped by owner).
+struct bgnn_part {
+  int device = 0;
+  uint32_t world = 1, rank = 0;
+  uint32_t n_global = 0;
+  std::vector<uint32_t> bounds;       // [world+1]
+  uint32_t lo = 0, hi = 0, n_own = 0, n_halo = 0;
+  uint64_t entry_lo = 0, n_local_entries = 0;  // the local rows' entries in the global CSR
+  bgnn_graph local;                   // [n_own rows, n_own + n_halo columns]
+  uint32_t* halo_ids = nullptr;       // [n_halo] global id of each halo slot
+  uint32_t* send_rows = nullptr;      // [n_send] owned rows (local ids) other ranks read, by peer
+  uint64_t n_send = 0;
+  std::vector<uint64_t> send_counts, recv_counts;  // rows per peer
+  std::vector<uint64_t> send_off, recv_off;        // exclusive prefix of the counts
+};
+void bgnn_part_free(bgnn_part* p);
+int bgnn_run_pack_cols(bgnn_ctx* ctx, const float* x, uint64_t ld_x, uint32_t col0,
+                       uint32_t width, const uint32_t* rows, uint64_t n, float* out);
+int bgnn_run_unpack_cols(bgnn_ctx* ctx, const float* src, uint64_t n, uint32_t width, float* x,
+                         uint64_t ld_x, uint32_t col0);
 
 // ---------------------------------------------------------------------------
 // error plumbing: every internal call returns a bgnn_status
@@ -140,6 +166,10 @@ int bgnn_graph_build(bgnn_ctx* ctx, const uint32_t* src_dev, const uint32_t* dst
                      uint64_t num_edges, uint32_t num_src, uint32_t num_dst, bgnn_graph* g);
 int bgnn_graph_from_csr(bgnn_ctx* ctx, const uint32_t* row_ptr, const uint32_t* col,
                         uint32_t num_rows, uint32_t num_cols, bgnn_graph* g, bool copy);
+// Takes ownership of a device CSR (cudaMalloc'd row_ptr [n_rows+1] and col
+// [nnz], already validated) and builds the row schedule.
+int bgnn_graph_adopt_csr(bgnn_ctx* ctx, uint32_t* row_ptr, uint32_t* col, uint32_t n_rows,
+                         uint32_t n_cols, uint64_t nnz, bgnn_graph* g);
 void bgnn_graph_free(bgnn_graph* g);
 int bgnn_graph_dinv(bgnn_ctx* ctx, bgnn_graph* g, int tail, const float** out);
 int bgnn_graph_dst_of(bgnn_ctx* ctx, bgnn_graph* g, const uint32_t** out);
@@ -182,6 +212,11 @@ struct AggArgs {
   int* err;               // device error word (set by the launcher)
 };
 int bgnn_run_aggregate(bgnn_ctx* ctx, int op, const AggArgs& a);
+// bgnn_aggregate / bgnn_graph_spmm (aggr BGNN_AGGR_SPMM) over a column slice
+// of x (row stride ld_x) into a column slice of out (row stride ld_out)
+int bgnn_run_aggregate_cols(bgnn_ctx* ctx, const bgnn_graph* g, int aggr, const float* values,
+                            const float* x, uint64_t ld_x, uint32_t width, float* out,
+                            uint64_t ld_out);
 
 // ---------------------------------------------------------------------------
 // GAT (gat.cu)
@@ -201,12 +236,6 @@ int bgnn_run_linear(bgnn_ctx* ctx, const float* a, const float* w, const float* 
 int bgnn_run_linear_add(bgnn_ctx* ctx, const float* a, const float* w, uint32_t m, uint32_t k,
                         uint32_t n, const float* addend, const float* bias, int act,
                         double act_param, float* out);
-// the same, with the rows of a remote map also stored into peers' buffers
-int bgnn_run_linear_add_remote(bgnn_ctx* ctx, const float* a, const float* w, uint32_t m,
-                               uint32_t k, uint32_t n, const float* addend, const float* bias,
-                               int act, double act_param, float* out, const uint32_t* row_ptr,
-                               const uint64_t* dst, float* const* peers,
-                               const uint32_t* peer_rows, uint32_t num_peers);
 int bgnn_run_activation(bgnn_ctx* ctx, int act, double param, const float* x, uint64_t n,
                         float* out);
 int bgnn_run_add(bgnn_ctx* ctx, const float* a, const float* b, uint64_t n, float* out);

@@ -386,6 +386,35 @@ extern "C" int bgnn_aggregate(bgnn_ctx* ctx, const bgnn_graph* g, int aggr, cons
   return bgnn_run_aggregate(ctx, aggr == BGNN_AGGR_MAX ? OP_MAX : OP_SUM, a);
 }
 
+int bgnn_run_aggregate_cols(bgnn_ctx* ctx, const bgnn_graph* g, int aggr, const float* values,
+                            const float* x, uint64_t ld_x, uint32_t width, float* out,
+                            uint64_t ld_out) {
+  AggArgs a = graph_args(g, x, width, out);
+  a.ld_x = (int64_t)ld_x;
+  a.ld_out = (int64_t)ld_out;
+  if (aggr == BGNN_AGGR_SPMM) {
+    a.val = values;
+    a.exact = ctx->math == BGNN_MATH_EXACT;
+    return bgnn_run_aggregate(ctx, OP_SPMM, a);
+  }
+  a.mean = aggr == BGNN_AGGR_MEAN;
+  a.max_fix = aggr == BGNN_AGGR_MAX;
+  return bgnn_run_aggregate(ctx, aggr == BGNN_AGGR_MAX ? OP_MAX : OP_SUM, a);
+}
+
+extern "C" int bgnn_aggregate_strided(bgnn_ctx* ctx, const bgnn_graph* g, int aggr,
+                                      const float* values, const float* x, uint64_t ld_x,
+                                      uint32_t width, float* out, uint64_t ld_out) {
+  BGNN_TRY(ctx_ok(ctx));
+  BGNN_REQUIRE(ctx, g != nullptr, "NULL graph");
+  BGNN_REQUIRE(ctx, aggr >= BGNN_AGGR_SUM && aggr <= BGNN_AGGR_SPMM, "unknown aggregation %d",
+               aggr);
+  BGNN_REQUIRE(ctx, ld_x >= width && ld_out >= width, "row strides must cover the width");
+  BGNN_REQUIRE(ctx, (x && out) || (uint64_t)g->n_dst * width == 0, "NULL x/out");
+  BGNN_REQUIRE(ctx, aggr != BGNN_AGGR_SPMM || values || g->num_edges == 0, "NULL values");
+  return bgnn_run_aggregate_cols(ctx, g, aggr, values, x, ld_x, width, out, ld_out);
+}
+
 extern "C" int bgnn_gcn_propagate(bgnn_ctx* ctx, const bgnn_graph* g, const float* h, uint32_t f,
                                   int add_self_loops, int normalize, const float* bias, int act,
                                   double act_param, float* out) {
@@ -495,20 +524,6 @@ extern "C" int bgnn_linear_add(bgnn_ctx* ctx, const float* a, const float* w, ui
   return bgnn_run_linear_add(ctx, a, w, m, k, n, addend, bias, act, act_param, out);
 }
 
-extern "C" int bgnn_linear_add_remote(bgnn_ctx* ctx, const float* a, const float* w, uint32_t m,
-                                      uint32_t k, uint32_t n, const float* addend,
-                                      const float* bias, int act, double act_param, float* out,
-                                      const uint32_t* row_ptr, const uint64_t* dst,
-                                      float* const* peers, const uint32_t* peer_rows,
-                                      uint32_t num_peers) {
-  BGNN_TRY(ctx_ok(ctx));
-  BGNN_TRY(check_act(ctx, act));
-  BGNN_REQUIRE(ctx, (a && w) || (uint64_t)m * k * n == 0, "NULL operand");
-  BGNN_REQUIRE(ctx, out || (uint64_t)m * n == 0, "NULL out");
-  BGNN_REQUIRE(ctx, row_ptr && peers && peer_rows && (dst || m == 0), "NULL remote map");
-  return bgnn_run_linear_add_remote(ctx, a, w, m, k, n, addend, bias, act, act_param, out,
-                                    row_ptr, dst, peers, peer_rows, num_peers);
-}
 
 extern "C" int bgnn_l2_normalize_rows(bgnn_ctx* ctx, float* x, uint32_t m, uint32_t n) {
   BGNN_TRY(ctx_ok(ctx));

@@ -66,31 +66,18 @@ constexpr size_t pg_smem_bytes() {
   return (size_t)PG_S * (PG_BK * (PG_BM + PG_APAD) + PG_BK * BN) * sizeof(float);
 }
 
-// Rows of the output that other GPUs also need: each row's values are
-// stored into the peers' buffers as well as C (plain stores through peer
-// mappings, no multicast).  dst[d] packs peer << 32 | destination row.
-struct RemoteRows {
-  const uint32_t* row_ptr = nullptr;  // [m+1] destination range of each output row
-  const uint64_t* dst = nullptr;
-  float* const* peers = nullptr;      // base of each peer's [rows, n] buffer
-  const uint32_t* peer_rows = nullptr;
-  uint32_t num_peers = 0;
-  int* err = nullptr;
-};
-
 // DUAL (the SAGE pair in one launch): the tile first runs A*B over k and
 // stores it, rounded to f32, into its own outputs of C (the reference's
 // St tensor); it then runs A2*B2 over k with that stored St as the addend,
 // i.e. C = act(f32(f32(St + A2*B2) + bias)), bit for bit what two launches
 // give, with one tile start-up and one launch instead of two.
-template <int BN, bool EXACT, bool B16, bool V4OUT, bool REMOTE = false, bool DUAL = false>
+template <int BN, bool EXACT, bool B16, bool V4OUT, bool DUAL = false>
 __global__ void __launch_bounds__(256, 2) k_sgemm_pipe(const float* __restrict__ A,
                                                        const float* __restrict__ B, uint32_t m,
                                                        uint32_t k, uint32_t n,
                                                        const float* addend,
                                                        const float* __restrict__ bias, int act,
                                                        double act_param, float* C,
-                                                       const RemoteRows rr,
                                                        const float* __restrict__ A2,
                                                        const float* __restrict__ B2) {
   constexpr int TN = BN / 16;                 // 8 or 4 columns per thread
@@ -378,42 +365,21 @@ __global__ void __launch_bounds__(256, 2) k_sgemm_pipe(const float* __restrict__
           for (int j = 0; j < 4; j++)
             if (gn + j < n) C[gm * n + gn + j] = v[j];
         }
-        if constexpr (REMOTE) {
-          const uint32_t d1 = rr.row_ptr[gm + 1];
-          for (uint32_t d = rr.row_ptr[gm]; d < d1; d++) {
-            const uint64_t dd = rr.dst[d];
-            const uint32_t p = (uint32_t)(dd >> 32), row = (uint32_t)dd;
-            if (p >= rr.num_peers || row >= rr.peer_rows[p] || rr.peers[p] == nullptr) {
-              dev_raise(rr.err, DEVERR_INDEX, d, 30);
-              continue;
-            }
-            float* q = rr.peers[p] + (uint64_t)row * n + gn;
-            if (V4OUT && gn + 3 < n) {
-              *reinterpret_cast<float4*>(q) = make_float4(v[0], v[1], v[2], v[3]);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 4; j++)
-                if (gn + j < n) q[j] = v[j];
-            }
-          }
-        }
       }
     }
   }
-  if constexpr (REMOTE) __threadfence_system();  // peer stores visible before the kernel ends
 }
 
-template <int BN, bool EXACT, bool B16, bool V4OUT, bool REMOTE = false, bool DUAL = false>
+template <int BN, bool EXACT, bool B16, bool V4OUT, bool DUAL = false>
 int launch_pipe_t(bgnn_ctx* ctx, const float* a, const float* b, uint32_t m, uint32_t k,
                   uint32_t n, const float* addend, const float* bias, int act, double act_param,
-                  float* out, const RemoteRows& rr = RemoteRows(), const float* a2 = nullptr,
-                  const float* b2 = nullptr) {
+                  float* out, const float* a2 = nullptr, const float* b2 = nullptr) {
   constexpr size_t smem = pg_smem_bytes<BN>();
-  auto kern = k_sgemm_pipe<BN, EXACT, B16, V4OUT, REMOTE, DUAL>;
+  auto kern = k_sgemm_pipe<BN, EXACT, B16, V4OUT, DUAL>;
   BGNN_CUDA(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)smem));
   dim3 grid((unsigned)((m + PG_BM - 1) / PG_BM), (n + BN - 1) / BN);
-  kern<<<grid, 256, smem, ctx->stream>>>(a, b, m, k, n, addend, bias, act, act_param, out, rr, a2,
+  kern<<<grid, 256, smem, ctx->stream>>>(a, b, m, k, n, addend, bias, act, act_param, out, a2,
                                          b2);
   BGNN_LAUNCHED(ctx);
   return BGNN_OK;
@@ -429,56 +395,25 @@ int launch_pipe(bgnn_ctx* ctx, const float* a, const float* b, uint32_t m, uint3
   const bool b16 = (n % 4 == 0) && ((uintptr_t)b % 16 == 0) && ((uintptr_t)b2 % 16 == 0);
   const bool v4 = (n % 4 == 0) && ((uintptr_t)out % 16 == 0) &&
                   (addend == nullptr || (uintptr_t)addend % 16 == 0);
-  const RemoteRows none;
   if (n <= 64) {
     if (b16)
-      return v4 ? launch_pipe_t<64, EXACT, true, true, false, DUAL>(
-                      ctx, a, b, m, k, n, addend, bias, act, act_param, out, none, a2, b2)
-                : launch_pipe_t<64, EXACT, true, false, false, DUAL>(
-                      ctx, a, b, m, k, n, addend, bias, act, act_param, out, none, a2, b2);
-    return launch_pipe_t<64, EXACT, false, false, false, DUAL>(
-        ctx, a, b, m, k, n, addend, bias, act, act_param, out, none, a2, b2);
+      return v4 ? launch_pipe_t<64, EXACT, true, true, DUAL>(
+                      ctx, a, b, m, k, n, addend, bias, act, act_param, out, a2, b2)
+                : launch_pipe_t<64, EXACT, true, false, DUAL>(
+                      ctx, a, b, m, k, n, addend, bias, act, act_param, out, a2, b2);
+    return launch_pipe_t<64, EXACT, false, false, DUAL>(
+        ctx, a, b, m, k, n, addend, bias, act, act_param, out, a2, b2);
   }
   if (b16)
-    return v4 ? launch_pipe_t<128, EXACT, true, true, false, DUAL>(
-                    ctx, a, b, m, k, n, addend, bias, act, act_param, out, none, a2, b2)
-              : launch_pipe_t<128, EXACT, true, false, false, DUAL>(
-                    ctx, a, b, m, k, n, addend, bias, act, act_param, out, none, a2, b2);
-  return launch_pipe_t<128, EXACT, false, false, false, DUAL>(
-      ctx, a, b, m, k, n, addend, bias, act, act_param, out, none, a2, b2);
+    return v4 ? launch_pipe_t<128, EXACT, true, true, DUAL>(
+                    ctx, a, b, m, k, n, addend, bias, act, act_param, out, a2, b2)
+              : launch_pipe_t<128, EXACT, true, false, DUAL>(
+                    ctx, a, b, m, k, n, addend, bias, act, act_param, out, a2, b2);
+  return launch_pipe_t<128, EXACT, false, false, DUAL>(
+      ctx, a, b, m, k, n, addend, bias, act, act_param, out, a2, b2);
 }
 
 }  // namespace
-
-// out = act(f32(f32(addend + a*w) + bias)), and every row listed in the
-// remote map also stored into the listed peer buffers (FAST math, n % 4 == 0,
-// 16-byte aligned operands)
-int bgnn_run_linear_add_remote(bgnn_ctx* ctx, const float* a, const float* w, uint32_t m,
-                               uint32_t k, uint32_t n, const float* addend, const float* bias,
-                               int act, double act_param, float* out, const uint32_t* row_ptr,
-                               const uint64_t* dst, float* const* peers,
-                               const uint32_t* peer_rows, uint32_t num_peers) {
-  if (m == 0 || n == 0) return BGNN_OK;
-  if (ctx->math == BGNN_MATH_EXACT)
-    return bgnn_set_error(ctx, BGNN_ERR_UNSUPPORTED, "peer stores run in the fast math mode only");
-  const bool aligned = (n % 4 == 0) && ((uintptr_t)w % 16 == 0) && ((uintptr_t)out % 16 == 0) &&
-                       (addend == nullptr || (uintptr_t)addend % 16 == 0);
-  if (!aligned)
-    return bgnn_set_error(ctx, BGNN_ERR_UNSUPPORTED,
-                          "peer stores need n %% 4 == 0 and 16-byte aligned w, out, addend");
-  RemoteRows rr;
-  rr.row_ptr = row_ptr;
-  rr.dst = dst;
-  rr.peers = peers;
-  rr.peer_rows = peer_rows;
-  rr.num_peers = num_peers;
-  rr.err = ctx->d_err;
-  if (n <= 64)
-    return launch_pipe_t<64, false, true, true, true>(ctx, a, w, m, k, n, addend, bias, act,
-                                                      act_param, out, rr);
-  return launch_pipe_t<128, false, true, true, true>(ctx, a, w, m, k, n, addend, bias, act,
-                                                     act_param, out, rr);
-}
 
 namespace {
 

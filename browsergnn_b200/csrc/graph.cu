@@ -292,6 +292,18 @@ int bgnn_graph_from_csr(bgnn_ctx* ctx, const uint32_t* row_ptr, const uint32_t* 
   return BGNN_OK;
 }
 
+int bgnn_graph_adopt_csr(bgnn_ctx* ctx, uint32_t* row_ptr, uint32_t* col, uint32_t n_rows,
+                         uint32_t n_cols, uint64_t nnz, bgnn_graph* g) {
+  g->device = ctx->device;
+  g->n_src = n_cols;
+  g->n_dst = n_rows;
+  g->num_edges = nnz;
+  g->csr_only = true;
+  g->row_ptr = row_ptr;
+  g->src_of = col;
+  return build_schedule(ctx, g);
+}
+
 int bgnn_graph_dinv(bgnn_ctx* ctx, bgnn_graph* g, int tail, const float** out) {
   float*& d = g->dinv[tail ? 1 : 0];
   if (!d) {

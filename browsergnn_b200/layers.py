@@ -310,6 +310,11 @@ class SAGEConv(Module):
         return agg
 
     def forward(self, input: GraphData, _act=None) -> GraphData:
+        if getattr(input, "pg", None) is not None:
+            # one rank's share of a row-partitioned graph (distributed.partition)
+            from .distributed import sage_forward
+
+            return sage_forward(self, input, _act)
         torch = _torch()
         dg, x = _prepare(self, input, self.inChannels, "SAGEConv")
         ctx = dg.ctx

@@ -65,7 +65,8 @@ typedef enum bgnn_math_mode { BGNN_MATH_FAST = 0, BGNN_MATH_EXACT = 1 } bgnn_mat
 typedef enum bgnn_aggr {
   BGNN_AGGR_SUM = 0,  /* wasmScatterAdd  src/backend/wasm/index.ts:70-105  */
   BGNN_AGGR_MEAN = 1, /* wasmScatterMean src/backend/wasm/index.ts:112-151 */
-  BGNN_AGGR_MAX = 2   /* wasmScatterMax  src/backend/wasm/index.ts:158-206 */
+  BGNN_AGGR_MAX = 2,  /* wasmScatterMax  src/backend/wasm/index.ts:158-206 */
+  BGNN_AGGR_SPMM = 3  /* per-entry values, wasmSpmm src/backend/wasm/index.ts:342-383 */
 } bgnn_aggr;
 
 typedef enum bgnn_act {
@@ -266,36 +267,6 @@ BGNN_API int bgnn_sage_linear(bgnn_ctx* ctx, const float* agg, const float* x, c
 BGNN_API int bgnn_linear_add(bgnn_ctx* ctx, const float* a, const float* w, uint32_t m,
                              uint32_t k, uint32_t n, const float* addend, const float* bias,
                              int act, double act_param, float* out);
-/* ---- peer buffers for bgnn_linear_add_remote (one process per GPU) ----
- * bgnn_shared_alloc: a device buffer of its own cudaMalloc allocation, so
- * its IPC handle (bgnn_ipc_handle, BGNN_IPC_HANDLE_BYTES bytes) maps it
- * from its first byte; another process of the node maps it with
- * bgnn_ipc_open (peer access enabled on demand) and unmaps it with
- * bgnn_ipc_close before the owner calls bgnn_shared_free. */
-#define BGNN_IPC_HANDLE_BYTES 64
-BGNN_API int bgnn_shared_alloc(bgnn_ctx* ctx, uint64_t bytes, void** out);
-BGNN_API int bgnn_shared_free(bgnn_ctx* ctx, void* p);
-BGNN_API int bgnn_ipc_handle(bgnn_ctx* ctx, void* base, uint8_t* handle_out);
-BGNN_API int bgnn_ipc_open(bgnn_ctx* ctx, const uint8_t* handle, void** out);
-BGNN_API int bgnn_ipc_close(bgnn_ctx* ctx, void* p);
-
-/* bgnn_linear_add for a row-partitioned graph on several GPUs of one node:
- * each output row is also stored into the [owned | halo] buffers of the
- * GPUs whose next layer reads it, so the next layer needs no all-to-all (the
- * store happens in the epilogue that produces the row).  row_ptr [m+1] and
- * dst (device arrays) list each row's destinations, dst packing
- * peer << 32 | destination row; peers[p] (a device array) is rank p's buffer
- * mapped into this process (CUDA IPC; plain stores, no multicast), rows of
- * width n, peer_rows[p] rows long.  A destination out of range is reported as
- * BGNN_ERR_OUT_OF_RANGE and skipped.  The caller orders the peers' reads
- * after this kernel on every rank (e.g. a collective on the same streams).
- * Fast math only; n % 4 == 0 and 16-byte aligned w, out and addend. */
-BGNN_API int bgnn_linear_add_remote(bgnn_ctx* ctx, const float* a, const float* w, uint32_t m,
-                                    uint32_t k, uint32_t n, const float* addend,
-                                    const float* bias, int act, double act_param, float* out,
-                                    const uint32_t* row_ptr, const uint64_t* dst,
-                                    float* const* peers, const uint32_t* peer_rows,
-                                    uint32_t num_peers);
 /* SAGE 'pool' aggregator projection (sage.ts:149-159) applied per node:
  * out[i,j] = f32(Math.max(0, bias[j] + sum_q x[i,q]*w[q,j])) with a double
  * accumulator; w is [k, k].  An edge's projected message depends only on its
@@ -319,6 +290,117 @@ BGNN_API int bgnn_segment_sum(bgnn_ctx* ctx, const float* x, uint32_t num_featur
 /* out[i,:] = x[rows[i],:]  (halo pack; same kernel as gather) */
 BGNN_API int bgnn_pack_rows(bgnn_ctx* ctx, const float* x, uint32_t num_x_rows, const uint32_t* rows,
                    uint32_t num_rows, uint32_t num_features, float* out);
+
+/* ---- row partition of a graph across the GPUs of one node ---------------
+ * No counterpart in the reference, which is single-device: these run the
+ * message passing of SAGEConv.forward (src/layers/sage.ts:113-217) and
+ * SparseCSR.matmul (src/core/sparse.ts:322-344) on several GPUs, one process
+ * per GPU.  Rank r owns the contiguous rows [lo, hi) of a square graph (about
+ * (E + N) / world entries plus rows each) and keeps their entries in the
+ * global order, so each row is reduced on one GPU exactly as on a single GPU.
+ * Every rank passes the same graph and derives the same plan on its device:
+ * no communication.  The local graph has n_own = hi - lo rows and
+ * n_own + n_halo columns: owned nodes first, then the halo nodes (the
+ * sorted unique remote columns the local rows read, grouped by owner).  A
+ * layer's input therefore lives in an [owned | halo] buffer of
+ * n_own + n_halo rows whose first n_own rows are this rank's. */
+typedef struct bgnn_part bgnn_part;
+/* From a graph's edge list ([src(E) | dst(E)], host or device): rows are
+ * destinations, each row's edges in COO order (the aggregation's order). */
+BGNN_API int bgnn_part_create(bgnn_ctx* ctx, const uint32_t* edge_index, uint64_t num_edges,
+                              uint32_t num_nodes, uint32_t world, uint32_t rank,
+                              int edge_index_on_host, bgnn_part** out);
+/* From a square device CSR (SparseCSR.fromCOO output): rows keep their
+ * entries in CSR order; the local entries are the global entries
+ * [entry_lo, entry_lo + num_local_entries), so per-entry values are the
+ * caller's value array offset by entry_lo. */
+BGNN_API int bgnn_part_create_csr(bgnn_ctx* ctx, const uint32_t* row_ptr, const uint32_t* col,
+                                  uint32_t num_rows, uint32_t world, uint32_t rank,
+                                  bgnn_part** out);
+BGNN_API int bgnn_part_destroy(bgnn_part* p);
+BGNN_API int bgnn_part_info(const bgnn_part* p, uint32_t* row_lo, uint32_t* row_hi,
+                            uint32_t* num_halo, uint64_t* entry_lo, uint64_t* num_local_entries,
+                            uint64_t* num_send);
+/* bounds: world + 1 row boundaries (host array) */
+BGNN_API int bgnn_part_bounds(const bgnn_part* p, uint32_t* bounds);
+/* rows this rank sends to / receives from each rank (host arrays of world) */
+BGNN_API int bgnn_part_counts(const bgnn_part* p, uint64_t* send_rows, uint64_t* recv_rows);
+/* the local graph (owned by the partition; valid until bgnn_part_destroy) */
+BGNN_API int bgnn_part_graph(const bgnn_part* p, const bgnn_graph** out);
+/* copies of the plan's lists (device buffers; either may be NULL): the
+ * global id of each halo slot [num_halo], and the owned rows (local ids)
+ * sent to the peers in peer order [num_send] */
+BGNN_API int bgnn_part_lists(bgnn_ctx* ctx, const bgnn_part* p, uint32_t* halo_ids,
+                             uint32_t* send_rows);
+/* out[i, :] = x[send_row[i], col0 : col0 + width] (x row stride ld_x) */
+BGNN_API int bgnn_part_pack(bgnn_ctx* ctx, const bgnn_part* p, const float* x, uint64_t ld_x,
+                            uint32_t col0, uint32_t width, float* out);
+/* x[n_own + i, col0 : col0 + width] = halo[i, :] for every halo row i */
+BGNN_API int bgnn_part_unpack(bgnn_ctx* ctx, const bgnn_part* p, const float* halo,
+                              uint32_t width, float* x, uint64_t ld_x, uint32_t col0);
+/* bgnn_aggregate / bgnn_graph_spmm (aggr BGNN_AGGR_SPMM, values per entry)
+ * over a column slice: x rows of stride ld_x, out rows of stride ld_out. */
+BGNN_API int bgnn_aggregate_strided(bgnn_ctx* ctx, const bgnn_graph* g, int aggr,
+                                    const float* values, const float* x, uint64_t ld_x,
+                                    uint32_t width, float* out, uint64_t ld_out);
+
+/* ---- NCCL halo exchange and distributed layers (one process per GPU) ----
+ * A bgnn_dist is one rank's NCCL communicator plus its streams.  Rank 0
+ * makes the unique id (bgnn_dist_unique_id) and the caller shares it with
+ * the other ranks by its own means.  Every call is asynchronous on the
+ * context's stream.  timeout_ms bounds every piece of NCCL work: when it is
+ * not done in time (a peer failed or never joined) the communicator is
+ * aborted and this and every later call on the object return
+ * BGNN_ERR_TIMEOUT.  max_ctas caps the CTAs NCCL uses (0: NCCL's default);
+ * the aggregation leaves that many SMs free while later chunks are in
+ * flight.  NCCL is loaded at run time (the copy already in the process, else
+ * libnccl.so.2 or $BGNN_NCCL_LIBRARY); without it these return
+ * BGNN_ERR_UNSUPPORTED. */
+#define BGNN_UNIQUE_ID_BYTES 128
+typedef struct bgnn_dist bgnn_dist;
+BGNN_API int bgnn_dist_unique_id(uint8_t* id_out);
+BGNN_API int bgnn_dist_create(bgnn_ctx* ctx, const uint8_t* unique_id, uint32_t world,
+                              uint32_t rank, uint32_t timeout_ms, uint32_t max_ctas,
+                              bgnn_dist** out);
+BGNN_API int bgnn_dist_destroy(bgnn_dist* d);
+/* Abort the communicator (a rank that learned on the host that a peer is
+ * gone): pending NCCL work ends, later calls return BGNN_ERR_DEVICE, and
+ * bgnn_dist_destroy then needs no peer. */
+BGNN_API int bgnn_dist_abort(bgnn_dist* d);
+/* column chunks of the pipelined exchange (0: by width, 4 at >= 192 columns,
+ * 2 at >= 96, else 1) and SMs left to NCCL while later chunks fly */
+BGNN_API int bgnn_dist_set_pipeline(bgnn_dist* d, uint32_t chunks, uint32_t reserve_sms);
+/* Fill the halo rows of x_ext ([n_own + n_halo, F], owned rows present)
+ * with their owners' rows. */
+BGNN_API int bgnn_dist_exchange(bgnn_dist* d, const bgnn_part* p, float* x_ext,
+                                uint32_t num_features);
+/* Halo exchange + fused gather/scatter (MessagePassing.scatter{Add,Mean,Max},
+ * sparse.ts:400-451) of the local rows: out [n_own, F].  The exchange runs
+ * in column chunks and each chunk's columns are aggregated as soon as it has
+ * landed; the halo rows of x_ext are filled as a side effect. */
+BGNN_API int bgnn_dist_aggregate(bgnn_dist* d, const bgnn_part* p, int aggr, float* x_ext,
+                                 uint32_t num_features, float* out);
+/* The same with per-entry values: the row-partitioned SparseCSR.matmul
+ * (sparse.ts:322-344 / wasmSpmm index.ts:342-383); values are the local
+ * entries' values (global values + entry_lo). */
+BGNN_API int bgnn_dist_spmm(bgnn_dist* d, const bgnn_part* p, const float* values, float* x_ext,
+                            uint32_t num_features, float* out);
+/* One SAGEConv layer (sage.ts:113-217) on the partition: x_ext [n_own +
+ * n_halo, k] with owned rows present; agg [n_own, k] scratch for the
+ * aggregation; out [n_own, n] = act(f32(f32(x*w_self + agg*w_neigh) + bias))
+ * (the roundings of bgnn_sage_linear; w_self NULL: rootWeight = false).
+ * x*w_self runs on a side stream while the halo rows are exchanged.  out may
+ * be the owned rows of the next layer's [owned | halo] buffer. */
+BGNN_API int bgnn_dist_sage_layer(bgnn_dist* d, const bgnn_part* p, int aggr, float* x_ext,
+                                  uint32_t k, uint32_t n, const float* w_neigh,
+                                  const float* w_self, const float* bias, int act,
+                                  double act_param, float* agg, float* out);
+/* Element-wise maximum over the ranks of count host doubles, in place
+ * (timing); synchronises. */
+BGNN_API int bgnn_dist_allreduce_max(bgnn_dist* d, double* values, uint32_t count);
+/* Wait for the context's stream, or for the timeout to abort the NCCL work
+ * it depends on (BGNN_ERR_TIMEOUT). */
+BGNN_API int bgnn_dist_synchronize(bgnn_dist* d);
 
 /* ---- benchmark inputs ------------------------------------------------------ */
 /* Seeded R-MAT edge list [src(E) | dst(E)] on the device (no reference

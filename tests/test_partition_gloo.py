@@ -1,7 +1,9 @@
-"""The N > 1 path on CPU: two gloo ranks build the row partition and halo plan
-(browsergnn_b200.partition.HaloPlan), exchange halo rows, and aggregate their
-rows with the oracle over the local CSR.  Every rank's rows must equal the
-single-process result bit for bit (each row keeps its COO edge order)."""
+"""The N > 1 path on CPU: gloo ranks each derive the row-partition plan
+(browsergnn_b200.partition.plan_rows, the host restatement of the device
+plan), exchange halo rows with the plan's counts, and aggregate their rows
+with the oracle over the local CSR.  Every rank's rows must equal the
+single-process result bit for bit (each row keeps its COO edge order), and
+the plans must agree across ranks without any exchange of requests."""
 import os
 import socket
 
@@ -24,53 +26,43 @@ def _rank_main(rank, world, port, n, f, ei, e, x, want, q):
     import torch
     import torch.distributed as dist
 
-    from browsergnn_b200.partition import HaloPlan
+    from browsergnn_b200 import partition
     from oracle import oracle as orc
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        t = torch.from_numpy(ei.view(np.int32).copy())
-        plan = HaloPlan(t[:e], t[e:], n, rank, world)
-        xl = torch.from_numpy(x[plan.lo:plan.hi].copy())
-
-        def pack(h, rows, out):  # CPU stand-in for bgnn_pack_rows
-            out.copy_(h.index_select(0, rows.long()))
-
-        ext = plan.exchange(xl, pack).numpy()
-        need = np.concatenate([np.arange(plan.lo, plan.hi), plan.halo.numpy()]).astype(np.int64)
-        ok_ext = np.array_equal(ext, x[need])
-        # in-place variant: owned rows already in the buffer, only halo rows move
-        buf = torch.full((plan.n_own + plan.n_halo, f), float("nan"))
-        buf[: plan.n_own].copy_(xl)
-        plan.exchange_into(buf, pack)
-        ok_ext = ok_ext and np.array_equal(buf.numpy(), x[need])
-        lei = plan.edge_index.numpy().view(np.uint32)
-        rp, so, _ = orc.dst_csr(np.concatenate([lei[:plan.num_edges], lei[plan.num_edges:]]),
-                                plan.num_edges, plan.n_own)
+        rp, so = partition.dst_csr(ei, e, n)
+        plan = partition.plan_rows(rp, so, world, rank)
+        # every rank derived the same bounds, and what p receives from r is
+        # what r sends to p, in the same (sorted id) order
+        plans = [None] * world
+        dist.all_gather_object(plans, (plan.bounds, plan.send_counts, plan.recv_counts,
+                                       (plan.send_rows + plan.lo).tolist(),
+                                       plan.halo_ids.tolist()))
+        ok_plan = all(p[0] == plan.bounds for p in plans)
+        for p in range(world):
+            if p == rank:
+                continue
+            bounds, sc_p, rc_p, send_p, halo_p = plans[p]
+            mine_from_p = [h for h in plan.halo_ids.tolist()
+                           if bounds[p] <= h < bounds[p + 1]]
+            off = sum(sc_p[:rank])
+            ok_plan = ok_plan and rc_p[rank] == plan.send_counts[p]
+            ok_plan = ok_plan and send_p[off:off + sc_p[rank]] == mine_from_p
+        ext = torch.full((plan.n_own + plan.n_halo, f), float("nan"))
+        ext[: plan.n_own] = torch.from_numpy(x[plan.lo:plan.hi])
+        partition.exchange(plan, ext)
+        need = np.concatenate([np.arange(plan.lo, plan.hi), plan.halo_ids]).astype(np.int64)
+        ok_ext = np.array_equal(ext.numpy(), x[need])
         res = {}
         for op in ("sum", "mean", "max"):
-            got = orc.csr_aggregate(rp, so, plan.n_own, ext, f, op, threads=1).reshape(-1, f)
+            got = orc.csr_aggregate(plan.row_ptr.astype(np.uint32), plan.col.astype(np.uint32),
+                                    plan.n_own, ext.numpy(), f, op, threads=1).reshape(-1, f)
             res[op] = np.array_equal(got.view(np.uint32),
                                      want[op][plan.lo:plan.hi].view(np.uint32))
-        # remote-store map: applying every rank's (peer, row) destinations to
-        # its owned rows must reproduce each rank's halo rows exactly
-        row_ptr, dst, peer_rows = plan.remote_map()
-        maps = [None] * world
-        dist.all_gather_object(maps, (plan.lo, plan.n_own, row_ptr.tolist(), dst.tolist(),
-                                      peer_rows))
-        buf = np.full((plan.n_own + plan.n_halo, f), np.nan, np.float32)
-        buf[: plan.n_own] = x[plan.lo:plan.hi]
-        ok_map = peer_rows[rank] == plan.n_own + plan.n_halo
-        for lo_p, n_own_p, rp_p, dst_p, _ in maps:
-            for i in range(n_own_p):
-                for d in dst_p[rp_p[i]:rp_p[i + 1]]:
-                    if (d >> 32) == rank:
-                        ok_map = ok_map and (d & 0xffffffff) >= plan.n_own
-                        buf[d & 0xffffffff] = x[lo_p + i]
-        ok_map = ok_map and np.array_equal(buf, x[need])
-        q.put((rank, ok_ext and ok_map, res, plan.n_own, plan.n_halo, plan.num_edges))
+        q.put((rank, ok_plan, ok_ext, res, plan.n_own, int(plan.col.size)))
     finally:
         dist.destroy_process_group()
 
@@ -97,9 +89,32 @@ def test_halo_partition_matches_single_process(world):
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     results = [q.get() for _ in range(world)]
     total_rows = total_edges = 0
-    for rank, ok_ext, res, n_own, n_halo, ne in results:
+    for rank, ok_plan, ok_ext, res, n_own, ne in results:
+        assert ok_plan, f"rank {rank}: plans disagree across ranks"
         assert ok_ext, f"rank {rank}: halo rows differ"
         assert all(res.values()), (rank, res)
         total_rows += n_own
         total_edges += ne
     assert total_rows == n and total_edges == e
+
+
+def test_plan_edge_cases():
+    """No edges (rows still balance), more ranks than rows, a hub row."""
+    from browsergnn_b200 import partition
+
+    rp = np.zeros(11, np.int64)
+    b = partition.row_bounds(rp, 3)
+    assert b[0] == 0 and b[-1] == 10 and all(b[i] <= b[i + 1] for i in range(3))
+    assert max(b[i + 1] - b[i] for i in range(3)) <= 4
+    rp2 = np.array([0, 1, 2], np.int64)
+    plans = [partition.plan_rows(rp2, np.array([1, 0]), 4, r) for r in range(4)]
+    assert sum(p.n_own for p in plans) == 2
+    for p in plans:
+        assert sum(p.recv_counts) == p.n_halo
+    # one hub row holding most edges gets a rank of its own
+    deg = np.array([5, 5, 1000, 5, 5, 5])
+    rp3 = np.concatenate([[0], np.cumsum(deg)])
+    col = np.random.default_rng(0).integers(0, 6, rp3[-1])
+    plans = [partition.plan_rows(rp3, col, 3, r) for r in range(3)]
+    owner = [r for r, p in enumerate(plans) if p.lo <= 2 < p.hi][0]
+    assert plans[owner].n_own <= 3
