@@ -263,6 +263,70 @@ def exchange_times(pg, dctx, reps):
     return res
 
 
+def layer_parts(layers, pg, dctx, reps):
+    """The pieces of a partitioned layer run one at a time on this rank's
+    share (ms, mean over reps, max over ranks): the aggregation over the
+    full width and over four column chunks, x * W_self and the fused
+    neighbour product.  Shows what the pipelined layer overlaps."""
+    import torch
+    import torch.distributed as dist
+
+    from browsergnn_b200.backend import ptr
+
+    ctx = pg.ctx
+    m = pg.n_own
+
+    def timed(fn):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / reps
+
+    out = {}
+    for li, lay in enumerate(layers):
+        k, n = lay.inChannels, lay.outChannels
+        ext = pg.ext_buffer(k)
+        ext.normal_()
+        agg = torch.empty((m, k), device="cuda")
+        st = torch.empty((m, n), device="cuda")
+        res = torch.empty((m, n), device="cuda")
+        step = (k + 3) // 4
+        step = (step + 3) & ~3
+        chunks = [(c0, min(step, k - c0)) for c0 in range(0, k, step)]
+
+        def agg_full():
+            ctx.call("bgnn_aggregate_strided", pg.graph, 1, None, ptr(ext), k, k, ptr(agg), k)
+
+        def agg_chunks():
+            for c0, w in chunks:
+                ctx.call("bgnn_aggregate_strided", pg.graph, 1, None, ptr(ext[:, c0:]), k, w,
+                         ptr(agg[:, c0:]), k)
+
+        def self_mm():
+            ctx.call("bgnn_linear", ptr(ext), ptr(lay.p("lin_self")), m, k, n, None, 0, 0.0,
+                     ptr(st))
+
+        def neigh_mm():
+            ctx.call("bgnn_linear_add", ptr(agg), ptr(lay.p("lin_neighbor")), m, k, n, ptr(st),
+                     ptr(lay.p("bias")), 1, 0.0, ptr(res))
+
+        v = [timed(agg_full), timed(agg_chunks), timed(self_mm), timed(neigh_mm)]
+        v = max_over_ranks(v)
+        out[f"L{li + 1}"] = {"aggregate_full_width": round(v[0], 3),
+                             f"aggregate_{len(chunks)}_chunks": round(v[1], 3),
+                             "x_w_self": round(v[2], 3), "agg_w_neigh_add": round(v[3], 3)}
+        del ext, agg, st, res
+    return out
+
+
 def e2e_single(layers, ei, x, n, e, warmup, steps):
     """The public API from pinned host buffers: GraphData from the step's
     host edge list and features (the edge list uploaded and the CSR built and
@@ -888,6 +952,9 @@ def main():
         dctx = distributed.DistContext(rank, world, device=local, timeout_ms=120_000)
         if args.chunks is not None:
             dctx.set_pipeline(args.chunks, args.reserve_sms)
+        torch.cuda.synchronize()
+        nccl_init_s = max_over_ranks(time.perf_counter() - t0)
+        t0 = time.perf_counter()
         pg = distributed.PartitionedGraph.from_edge_index(ei, e, n, world, rank, device=local)
         ext0 = pg.ext_buffer(WIDTHS[0])
         ext0[: pg.n_own].copy_(x_full[pg.lo:pg.hi])
@@ -983,6 +1050,8 @@ def main():
     exchange_only = None
     if world > 1:
         exchange_only = exchange_times(pgd.pg, dctx, max(3, args.steps // 2))
+        exchange_only["parts_of_a_layer"] = layer_parts(layers, pgd.pg, dctx,
+                                                        max(3, args.steps // 2))
 
     # e2e through the public API: host features + host edge index each step
     e2e = None
@@ -1044,6 +1113,7 @@ def main():
                        "parallelism": f"row-partition x{world}" if world > 1 else "single",
                        "l2": "inputs larger than L2 (no flush)", "math": "fast (f32 fma)",
                        "graph_build_s": round(build_s, 3)},
+            "nccl_init_s": round(nccl_init_s, 3) if world > 1 else None,
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
             "clocks": clocks, "gpu_launches": launches,
             "phase_ms_max_over_ranks": phase_ms,

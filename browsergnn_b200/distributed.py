@@ -153,7 +153,10 @@ class PartitionedGraph:
             ctx.call("bgnn_part_create", ptr(ei), int(num_edges), int(num_nodes), int(world),
                      int(rank), 0, ctypes.byref(h))
         else:
-            ei = np.ascontiguousarray(np.asarray(edge_index, dtype=np.uint32))
+            if isinstance(edge_index, torch.Tensor):  # host tensor: no copy, keep pinned memory
+                ei = edge_index.contiguous().numpy().view(np.uint32)
+            else:
+                ei = np.ascontiguousarray(np.asarray(edge_index, dtype=np.uint32))
             ctx.call("bgnn_part_create", ei.ctypes.data if ei.size else None, int(num_edges),
                      int(num_nodes), int(world), int(rank), 1, ctypes.byref(h))
         return cls(h, ctx, world, rank)
