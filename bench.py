@@ -785,13 +785,15 @@ def cpu_sample_forward(threads, frac=64, repeats=1):
     return 3 * w.num_edges / t, desc, w.num_edges, t
 
 
-def profile_case(kind):
+def profile_case(kind, math="fast"):
     """Small, self-contained launches for ncu (profiles/ cites these):
     small    : R-MAT 1,000,000 nodes / 25,000,000 edges, F=256: one mean
                aggregation, then one SAGE linear 256 -> 256 (two SGEMM launches)
     full-agg : the benchmark graph (2,450,000 / 62,000,000), F=256 mean
                aggregation twice (capture the second)
-    csr      : SparseCSR.fromCOO of the SpMM workload (2^28 entries), twice."""
+    csr      : SparseCSR.fromCOO of the SpMM workload (2^28 entries), twice
+    linear   : the SAGE pair 256 -> 256 on 1,000,000 rows, three times (pass
+               --math tensor for the tcgen05 kernel)."""
     import torch
 
     import browsergnn_b200 as bg
@@ -801,6 +803,29 @@ def profile_case(kind):
 
     bg.init_browsergnn()
     ctx = bg.get_context()
+    ctx.set_math(math)
+    if kind == "linear":
+        # the SAGE pair 256 -> 256 on 1,000,000 rows (2 x 131 GFLOP), three times
+        m, k, nn = 1_000_000, 256, 256
+        gen = torch.Generator("cuda").manual_seed(3)
+        x = torch.randn((m, k), device="cuda", generator=gen)
+        agg = torch.randn((m, k), device="cuda", generator=gen)
+        ws = torch.randn((k, nn), device="cuda", generator=gen) * 0.06
+        wn = torch.randn((k, nn), device="cuda", generator=gen) * 0.06
+        b = torch.randn(nn, device="cuda", generator=gen)
+        out = torch.empty((m, nn), device="cuda")
+        for _ in range(3):
+            a0 = torch.cuda.Event(enable_timing=True)
+            a1 = torch.cuda.Event(enable_timing=True)
+            a0.record()
+            ctx.call("bgnn_sage_linear", ptr(agg), ptr(x), ptr(wn), ptr(ws), m, k, nn, ptr(b), 1,
+                     0.0, ptr(out))
+            a1.record()
+            torch.cuda.synchronize()
+            ms = a0.elapsed_time(a1)
+            print(f"sage_linear ({math}) {m}x{k} -> {nn}: {ms:.3f} ms, "
+                  f"{4 * m * k * nn / (ms * 1e-3) / 1e12:.1f} TFLOP/s of the f32 products")
+        return
     if kind == "csr":
         # SparseCSR.fromCOO of the SpMM workload's 2^28 entries, twice
         n, e = 1 << synth.SPMM_SCALE, synth.SPMM_E
@@ -893,15 +918,19 @@ def main():
     ap.add_argument("--no-small", action="store_true")
     ap.add_argument("--no-parity", action="store_true",
                     help="skip the full-size output checks (oracle at N=1, N=1 bits at N>1)")
+    ap.add_argument("--math", choices=["fast", "tensor"], default="fast",
+                    help="fast: X*W on the FP32 pipe in the reference's order (the parity mode); "
+                         "tensor: X*W on the tcgen05 tensor cores (3xTF32), with the count of "
+                         "elements outside the parity bar reported")
     ap.add_argument("--chunks", type=int, default=None,
                     help="N>1: column chunks of the pipelined halo exchange (0: by width)")
     ap.add_argument("--reserve-sms", type=int, default=16,
                     help="N>1: SMs the aggregation leaves to NCCL while chunks are in flight")
-    ap.add_argument("--profile", choices=["small", "full-agg", "csr"], default=None,
+    ap.add_argument("--profile", choices=["small", "full-agg", "csr", "linear"], default=None,
                     help="run one profiling case for ncu and exit")
     args = ap.parse_args()
     if args.profile:
-        profile_case(args.profile)
+        profile_case(args.profile, args.math)
         return
     rank = env_int("RANK", 0)
     world = env_int("WORLD_SIZE", 1)
@@ -933,6 +962,7 @@ def main():
                                 device_id=torch.device(f"cuda:{local}"), pg_options=opts)
     bg.init_browsergnn({"device": local})
     ctx = bg.get_context(local)
+    ctx.set_math(args.math)
     hbm_peak, peak_kind = peaks()
 
     n, e, scale = synth.SAGE_N, synth.SAGE_E, synth.SAGE_SCALE
@@ -1111,7 +1141,9 @@ def main():
             "config": {"workload": "sage-mean-3layer-rmat-2450000n-62000000e",
                        "widths": WIDTHS, "edges_per_layer": e, "layers": 3,
                        "parallelism": f"row-partition x{world}" if world > 1 else "single",
-                       "l2": "inputs larger than L2 (no flush)", "math": "fast (f32 fma)",
+                       "l2": "inputs larger than L2 (no flush)",
+                       "math": ("fast (f32 fma in the reference's order)" if args.math == "fast"
+                                else "tensor (X*W on tcgen05, 3xTF32)"),
                        "graph_build_s": round(build_s, 3)},
             "nccl_init_s": round(nccl_init_s, 3) if world > 1 else None,
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,

@@ -15,7 +15,7 @@ LIB_PATH = os.path.join(_PKG, "libbgnn_cuda.so")
 # bgnn_status
 OK, ERR_INVALID_ARG, ERR_OUT_OF_RANGE, ERR_CUDA, ERR_NO_MEMORY, ERR_TIMEOUT, ERR_UNSUPPORTED, \
     ERR_DEVICE = range(8)
-MATH_FAST, MATH_EXACT = 0, 1
+MATH_FAST, MATH_EXACT, MATH_TENSOR = 0, 1, 2
 AGGR = {"sum": 0, "add": 0, "mean": 1, "max": 2}
 AGGR_SPMM = 3
 ACT = {None: 0, "none": 0, "relu": 1, "relu_max": 2, "elu": 3, "leaky_relu": 4, "sigmoid": 5,

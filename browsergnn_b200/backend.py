@@ -62,10 +62,21 @@ class CudaContext:
         rc = getattr(self.lib, name)(*args)
         _lib.check(rc, self.h)
 
-    def set_math(self, exact: bool):
-        mode = _lib.MATH_EXACT if exact else _lib.MATH_FAST
-        _lib.check(self.lib.bgnn_ctx_set_math(self.h, mode), self.h)
-        self._math = mode
+    def set_math(self, mode):
+        """True / "exact": the reference's rounding, bit for bit; False /
+        "fast": f32 fma in the reference's order (the default); "tensor":
+        X*W on the tcgen05 tensor cores (3xTF32, f32-level accuracy, not
+        the reference's summation order)."""
+        if mode is True or mode == "exact":
+            code = _lib.MATH_EXACT
+        elif mode is False or mode is None or mode == "fast":
+            code = _lib.MATH_FAST
+        elif mode == "tensor":
+            code = _lib.MATH_TENSOR
+        else:
+            raise ValueError(f"unknown math mode {mode!r}")
+        _lib.check(self.lib.bgnn_ctx_set_math(self.h, code), self.h)
+        self._math = code
 
     @property
     def exact(self) -> bool:

@@ -236,6 +236,14 @@ int bgnn_run_linear(bgnn_ctx* ctx, const float* a, const float* w, const float* 
 int bgnn_run_linear_add(bgnn_ctx* ctx, const float* a, const float* w, uint32_t m, uint32_t k,
                         uint32_t n, const float* addend, const float* bias, int act,
                         double act_param, float* out);
+// out = act(f32(f32(addend + a1*w1 + a2*w2) + bias)) on the tcgen05 tensor
+// cores (3xTF32, one f32 accumulator per output); a2/w2 optional (k2 = 0).
+// BGNN_ERR_UNSUPPORTED (no error recorded) when the operands do not suit
+// TMA (row lengths not a multiple of 4, unaligned bases): use the FP32 path.
+int bgnn_run_linear_tc(bgnn_ctx* ctx, const float* a1, const float* w1, uint32_t k1,
+                       const float* a2, const float* w2, uint32_t k2, uint32_t m, uint32_t n,
+                       const float* addend, const float* bias, int act, double act_param,
+                       float* out);
 int bgnn_run_activation(bgnn_ctx* ctx, int act, double param, const float* x, uint64_t n,
                         float* out);
 int bgnn_run_add(bgnn_ctx* ctx, const float* a, const float* b, uint64_t n, float* out);

@@ -145,7 +145,7 @@ extern "C" int bgnn_ctx_set_stream(bgnn_ctx* ctx, void* s) {
 
 extern "C" int bgnn_ctx_set_math(bgnn_ctx* ctx, int mode) {
   if (!ctx) return BGNN_ERR_INVALID_ARG;
-  if (mode != BGNN_MATH_FAST && mode != BGNN_MATH_EXACT)
+  if (mode != BGNN_MATH_FAST && mode != BGNN_MATH_EXACT && mode != BGNN_MATH_TENSOR)
     return bgnn_set_error(ctx, BGNN_ERR_INVALID_ARG, "unknown math mode %d", mode);
   ctx->math = mode;
   return BGNN_OK;

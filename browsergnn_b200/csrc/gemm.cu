@@ -512,6 +512,11 @@ int bgnn_run_linear(bgnn_ctx* ctx, const float* a, const float* w, const float* 
   // k == 0 runs no mac step: the output is act(0 + bias), as in the reference
   const bool dual = a2 != nullptr && w2 != nullptr;
   const bool exact = ctx->math == BGNN_MATH_EXACT;
+  if (ctx->math == BGNN_MATH_TENSOR && k > 0) {
+    const int rc = bgnn_run_linear_tc(ctx, a, w, k, dual ? a2 : nullptr, dual ? w2 : nullptr,
+                                      dual ? k : 0, m, n, nullptr, bias, act, act_param, out);
+    if (rc != BGNN_ERR_UNSUPPORTED) return rc;
+  }
   // SAGE pair: St = a2*w2 stored as f32 (the reference's Tensor), then
   // f32(St + a*w) (+ bias, activation); one launch runs both products per
   // output tile (k == 0 keeps two launches: the first writes St = 0)
@@ -533,6 +538,11 @@ int bgnn_run_linear_add(bgnn_ctx* ctx, const float* a, const float* w, uint32_t 
                         uint32_t n, const float* addend, const float* bias, int act,
                         double act_param, float* out) {
   if (m == 0 || n == 0) return BGNN_OK;
+  if (ctx->math == BGNN_MATH_TENSOR && k > 0) {
+    const int rc = bgnn_run_linear_tc(ctx, a, w, k, nullptr, nullptr, 0, m, n, addend, bias, act,
+                                      act_param, out);
+    if (rc != BGNN_ERR_UNSUPPORTED) return rc;
+  }
   return ctx->math == BGNN_MATH_EXACT
              ? launch_pipe<true>(ctx, a, w, m, k, n, addend, bias, act, act_param, out)
              : launch_pipe<false>(ctx, a, w, m, k, n, addend, bias, act, act_param, out);

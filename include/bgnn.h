@@ -60,7 +60,18 @@ typedef enum bgnn_status {
   BGNN_ERR_DEVICE = 7         /* a kernel raised its error flag              */
 } bgnn_status;
 
-typedef enum bgnn_math_mode { BGNN_MATH_FAST = 0, BGNN_MATH_EXACT = 1 } bgnn_math_mode;
+/* BGNN_MATH_TENSOR: as BGNN_MATH_FAST, except that the dense X*W products
+ * (bgnn_linear, bgnn_sage_linear, bgnn_linear_add, matmul) run on the
+ * tcgen05 tensor cores with a 3xTF32 split: f32-level accuracy but not the
+ * reference's k-ascending f32 rounding sequence, so an element whose
+ * reference value is a near-cancellation can fall outside the element-wise
+ * 1e-6 + 1e-5|ref| bar.  Operands whose row length is not a multiple of 4
+ * fall back to the FAST kernel. */
+typedef enum bgnn_math_mode {
+  BGNN_MATH_FAST = 0,
+  BGNN_MATH_EXACT = 1,
+  BGNN_MATH_TENSOR = 2
+} bgnn_math_mode;
 
 typedef enum bgnn_aggr {
   BGNN_AGGR_SUM = 0,  /* wasmScatterAdd  src/backend/wasm/index.ts:70-105  */
