@@ -792,8 +792,13 @@ def profile_case(kind, math="fast"):
     full-agg : the benchmark graph (2,450,000 / 62,000,000), F=256 mean
                aggregation twice (capture the second)
     csr      : SparseCSR.fromCOO of the SpMM workload (2^28 entries), twice
+    csr-small: SparseCSR.fromCOO of 2^25 entries (scale-21 R-MAT), twice
     linear   : the SAGE pair 256 -> 256 on 1,000,000 rows, three times (pass
-               --math tensor for the tcgen05 kernel)."""
+               --math tensor for the tcgen05 kernel)
+    gat      : the 2-layer GAT workload (20,000 nodes / 200,000 edges), three
+               forwards
+    spmm-small: the SpMM on a scale-21 R-MAT matrix (2^25 entries) at F = 32,
+               64, 128, 256."""
     import torch
 
     import browsergnn_b200 as bg
@@ -825,6 +830,64 @@ def profile_case(kind, math="fast"):
             ms = a0.elapsed_time(a1)
             print(f"sage_linear ({math}) {m}x{k} -> {nn}: {ms:.3f} ms, "
                   f"{4 * m * k * nn / (ms * 1e-3) / 1e12:.1f} TFLOP/s of the f32 products")
+        return
+    if kind == "gat":
+        # the 2-layer GAT workload (20,000 nodes, 200,000 edges, 500 -> 8x8 ->
+        # 16), three forwards
+        w = synth.gat_rmat()
+        rng = np.random.default_rng(7)
+        l1 = bg.GATConv(inChannels=500, outChannels=8, heads=8)
+        l1.loadStateDict({"weight": synth.glorot(500, 64, rng),
+                          "att_src": (0.3 * rng.standard_normal((8, 8))).astype(np.float32),
+                          "att_dst": (0.3 * rng.standard_normal((8, 8))).astype(np.float32),
+                          "bias": rng.uniform(-0.1, 0.1, 64).astype(np.float32)})
+        l2 = bg.GATConv(inChannels=64, outChannels=16, heads=1)
+        l2.loadStateDict({"weight": synth.glorot(64, 16, rng),
+                          "att_src": (0.3 * rng.standard_normal((1, 16))).astype(np.float32),
+                          "att_dst": (0.3 * rng.standard_normal((1, 16))).astype(np.float32),
+                          "bias": rng.uniform(-0.1, 0.1, 16).astype(np.float32)})
+        g = bg.GraphData(x=w.x, numNodes=w.num_nodes, numFeatures=500, edgeIndex=w.edge_index,
+                         numEdges=w.num_edges)
+        for _ in range(3):
+            out = l2.forward(l1.forward(g, _act="elu")).x
+        torch.cuda.synchronize()
+        print(f"GAT forward done, output {tuple(out.shape)}")
+        return
+    if kind == "spmm-small":
+        # the SpMM sweep on a scale-21 R-MAT matrix (2,097,152 rows, 2^25
+        # entries): one launch per width F = 32 / 64 / 128 / 256
+        scale = 21
+        n, e = 1 << scale, 1 << 25
+        ei = synth.rmat_edges_gpu(scale, n, e, synth.seed_for(5))
+        vals = torch.rand(e, device="cuda", generator=torch.Generator("cuda").manual_seed(2))
+        csr = bg.SparseCSR.fromCOO(bg.SparseCOO(ei[:e], ei[e:], vals, (n, n)))
+        del ei
+        gen = torch.Generator("cuda").manual_seed(3)
+        for f in (32, 64, 128, 256):
+            x = torch.randn((n, f), device="cuda", generator=gen)
+            a0 = torch.cuda.Event(enable_timing=True)
+            a1 = torch.cuda.Event(enable_timing=True)
+            a0.record()
+            csr.matmul(x)
+            a1.record()
+            torch.cuda.synchronize()
+            print(f"spmm F={f}: {a0.elapsed_time(a1):.3f} ms")
+        return
+    if kind == "csr-small":
+        # SparseCSR.fromCOO of 2^25 entries (scale-21 R-MAT), twice
+        scale = 21
+        n, e = 1 << scale, 1 << 25
+        ei = synth.rmat_edges_gpu(scale, n, e, synth.seed_for(5))
+        vals = torch.ones(e, device="cuda")
+        for _ in range(2):
+            a0 = torch.cuda.Event(enable_timing=True)
+            a1 = torch.cuda.Event(enable_timing=True)
+            a0.record()
+            csr = bg.SparseCSR.fromCOO(bg.SparseCOO(ei[:e], ei[e:], vals, (n, n)))
+            a1.record()
+            torch.cuda.synchronize()
+            print(f"fromCOO {e} entries: {a0.elapsed_time(a1):.3f} ms")
+            del csr
         return
     if kind == "csr":
         # SparseCSR.fromCOO of the SpMM workload's 2^28 entries, twice
@@ -926,7 +989,8 @@ def main():
                     help="N>1: column chunks of the pipelined halo exchange (0: by width)")
     ap.add_argument("--reserve-sms", type=int, default=16,
                     help="N>1: SMs the aggregation leaves to NCCL while chunks are in flight")
-    ap.add_argument("--profile", choices=["small", "full-agg", "csr", "linear"], default=None,
+    ap.add_argument("--profile", choices=["small", "full-agg", "csr", "csr-small", "linear", "gat",
+                                          "spmm-small"], default=None,
                     help="run one profiling case for ncu and exit")
     args = ap.parse_args()
     if args.profile:
