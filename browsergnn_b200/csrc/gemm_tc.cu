@@ -8,10 +8,17 @@
 // path therefore runs only in the BGNN_MATH_TENSOR mode; the default keeps
 // X*W on the FP32 pipe in the reference's order (gemm.cu).
 //
+// Accumulation: the tensor core adds its products into the f32 accumulator
+// with its own rounding, and over a whole K that error reaches the size of
+// the 1e-5 relative bar (measured: 3.9% of a SAGE layer's elements outside
+// it).  So each 32-wide k block goes into its own tensor-memory buffer (four
+// in rotation) and the epilogue warps add the block's partial sums into f32
+// registers with round-to-nearest ("promotion"): the tensor core then only
+// ever sums 12 products.
+//
 // Schedule: a persistent kernel, one CTA per SM, 128-row output tiles of
-// NT columns (NT = the output width rounded up to 16, at most 256), walked
-// tile by tile with two accumulators in tensor memory so the epilogue of one
-// tile overlaps the main loop of the next.  Warp roles:
+// NT columns (NT = the output width rounded up to 16, at most 128: the
+// epilogue holds a row's NT sums in registers).  Warp roles:
 //   warp 8     TMA producer: per 32-wide k block, the A rows (128 x 32 f32,
 //              128-byte swizzle) and the pre-split B_hi / B_lo tiles
 //              (NT x 32, K-major) into a ring of shared-memory stages;
@@ -19,10 +26,11 @@
 //              A_lo beside it (same offsets, so the swizzle carries over),
 //              then fences the generic-proxy writes for the tensor core;
 //   warp 9     MMA issuer (one thread): 3 x 4 tcgen05.mma (M=128, N=NT,
-//              K=8) per k block, a tcgen05.commit frees the stage, another
-//              marks the accumulator full after the last k block;
-//   warps 0-3  epilogue: tcgen05.ld of its 32 accumulator lanes (rows),
-//              f32(addend + acc), + bias, activation, stores.
+//              K=8) per k block into the block's tensor-memory buffer; one
+//              tcgen05.commit frees the stage, another marks the buffer full;
+//   warps 0-3  epilogue: per k block, tcgen05.ld of its 32 lanes (rows) of
+//              the buffer and f32 adds into registers; after the last block
+//              f32(addend + sum), + bias, activation, stores.
 // Every mbarrier wait is bounded; a wait that gives up raises the context's
 // error word (BGNN_ERR_TIMEOUT at the next synchronisation), tells the other
 // roles through shared memory and the CTA frees its tensor memory and exits.
@@ -42,14 +50,17 @@ constexpr int TC_BK = 32;                     // f32 per k block: one 128-byte s
 constexpr int TC_THREADS = 320;               // 10 warps
 constexpr uint32_t TC_SPIN_LIMIT = 1u << 24;  // try_wait polls before a wait gives up
 
+constexpr int TC_BUFS = 4;  // k-block accumulators in tensor memory
+
 template <int NT>
 struct TcCfg {
-  static constexpr int STAGES = NT >= 256 ? 2 : (NT >= 128 ? 3 : 4);
+  static_assert(NT % 16 == 0 && NT <= 128, "tile width");
+  static constexpr int STAGES = NT >= 128 ? 3 : 4;
   static constexpr int A_BYTES = TC_BM * TC_BK * 4;  // 16 KB
   static constexpr int B_BYTES = NT * TC_BK * 4;
   static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
-  static constexpr int TMEM_COLS = 2 * NT <= 32 ? 32 : 2 * NT <= 64 ? 64 : 2 * NT <= 128 ? 128
-                                 : 2 * NT <= 256 ? 256 : 512;
+  static constexpr int TMEM_COLS = TC_BUFS * NT <= 32 ? 32 : TC_BUFS * NT <= 64 ? 64
+                                 : TC_BUFS * NT <= 128 ? 128 : TC_BUFS * NT <= 256 ? 256 : 512;
   static constexpr uint32_t TX = A_BYTES + 2 * B_BYTES;  // bytes the TMA brings per stage
   static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
   static_assert(B_BYTES % 1024 == 0, "every operand tile starts on a 1024-byte swizzle atom");
@@ -169,10 +180,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint8_t* gbase = tc_smem + (base - raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(gbase + (size_t)S * C::STAGE_BYTES);
   // full[S] (TMA landed), split[S] (A split), empty[S] (MMAs done with the
-  // stage), accf[2] (accumulator ready), acce[2] (accumulator drained)
+  // stage), accf[B] (k-block partials ready), acce[B] (partials drained)
   const uint32_t b_full = s_addr(bars), b_split = b_full + 8 * S, b_empty = b_split + 8 * S;
-  const uint32_t b_accf = b_empty + 8 * S, b_acce = b_accf + 16;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 4);
+  const uint32_t b_accf = b_empty + 8 * S, b_acce = b_accf + 8 * TC_BUFS;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 2 * TC_BUFS);
   volatile uint32_t* abort_flag = tmem_slot + 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -182,7 +193,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       mbar_init(b_split + 8 * s, 128);
       mbar_init(b_empty + 8 * s, 1);
     }
-    for (int b = 0; b < 2; b++) {
+    for (int b = 0; b < TC_BUFS; b++) {
       mbar_init(b_accf + 8 * b, 1);
       mbar_init(b_acce + 8 * b, 128);
     }
@@ -234,16 +245,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   } else if (warp == 9) {
     // ---- MMA issuer ----
     if (lane == 0 && nkb > 0) {
-      int s = 0;
+      int s = 0, buf = 0;
       uint32_t ph = 0, aph = 0;
-      int buf = 0;
       for (uint32_t t = blockIdx.x; t < tiles; t += gridDim.x) {
-        if (!mbar_wait(b_acce + 8 * buf, aph ^ 1u, abort_flag, a.err, 51)) goto done;
-        tc_fence_after();
-        const uint32_t d = tmem + (uint32_t)(buf * NT);
         for (uint32_t kb = 0; kb < nkb; kb++) {
+          if (!mbar_wait(b_acce + 8 * buf, aph ^ 1u, abort_flag, a.err, 51)) goto done;
           if (!mbar_wait(b_split + 8 * s, ph, abort_flag, a.err, 52)) goto done;
           tc_fence_after();
+          const uint32_t d = tmem + (uint32_t)(buf * NT);
           const uint32_t st = stage_addr(s);
 #pragma unroll
           for (int kk = 0; kk < TC_BK / 8; kk++) {
@@ -251,20 +260,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const uint64_t ah = smem_desc(st + off), al = smem_desc(st + C::A_BYTES + off);
             const uint64_t bh = smem_desc(st + 2 * C::A_BYTES + off);
             const uint64_t bl = smem_desc(st + 2 * C::A_BYTES + C::B_BYTES + off);
-            mma_tf32(d, al, bh, C::IDESC, (kb | (uint32_t)kk) != 0u);
+            // small terms first; the block's first product starts the buffer
+            mma_tf32(d, al, bh, C::IDESC, kk != 0 ? 1u : 0u);
             mma_tf32(d, ah, bl, C::IDESC, 1u);
             mma_tf32(d, ah, bh, C::IDESC, 1u);
           }
           mma_commit(b_empty + 8 * s);
+          mma_commit(b_accf + 8 * buf);
           if (++s == S) {
             s = 0;
             ph ^= 1u;
           }
-        }
-        mma_commit(b_accf + 8 * buf);
-        if (++buf == 2) {
-          buf = 0;
-          aph ^= 1u;
+          if (++buf == TC_BUFS) {
+            buf = 0;
+            aph ^= 1u;
+          }
         }
       }
     }
@@ -311,62 +321,60 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     for (uint32_t t = blockIdx.x; t < tiles; t += gridDim.x) {
       const uint32_t m0 = (t / n_tiles) * TC_BM, n0 = (t % n_tiles) * NT;
       const uint32_t row = m0 + (uint32_t)threadIdx.x;
-      if (nkb > 0) {
+      float acc[NT];
+#pragma unroll
+      for (int j = 0; j < NT; j++) acc[j] = 0.0f;
+      for (uint32_t kb = 0; kb < nkb; kb++) {
         if (!mbar_wait(b_accf + 8 * buf, aph, abort_flag, a.err, 54)) goto done;
         tc_fence_after();
-      }
-#pragma unroll 1
-      for (int c = 0; c < NT / 16; c++) {
-        float v[16];
-        if (nkb > 0) {
-          tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(buf * NT + c * 16), v);
-        } else {
+        const uint32_t tb = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(buf * NT);
 #pragma unroll
-          for (int j = 0; j < 16; j++) v[j] = 0.0f;
-        }
-        const uint32_t col0 = n0 + (uint32_t)c * 16u;
-        if (row >= a.m || col0 >= a.n) continue;
-        float* o = a.out + (uint64_t)row * a.n + col0;
-        const float* ad = a.addend ? a.addend + (uint64_t)row * a.n + col0 : nullptr;
-        if (v4 && col0 + 16u <= a.n) {
+        for (int c = 0; c < NT / 16; c++) {
+          float v[16];
+          tmem_ld16(tb + (uint32_t)(c * 16), v);
 #pragma unroll
-          for (int q = 0; q < 4; q++) {
-            float4 x = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-            if (ad) {
-              const float4 y = *reinterpret_cast<const float4*>(ad + 4 * q);
-              x.x = __fadd_rn(y.x, x.x);
-              x.y = __fadd_rn(y.y, x.y);
-              x.z = __fadd_rn(y.z, x.z);
-              x.w = __fadd_rn(y.w, x.w);
-            }
-            if (a.bias) {
-              x.x = __fadd_rn(x.x, a.bias[col0 + 4 * q]);
-              x.y = __fadd_rn(x.y, a.bias[col0 + 4 * q + 1]);
-              x.z = __fadd_rn(x.z, a.bias[col0 + 4 * q + 2]);
-              x.w = __fadd_rn(x.w, a.bias[col0 + 4 * q + 3]);
-            }
-            x.x = apply_act(x.x, a.act, a.act_param);
-            x.y = apply_act(x.y, a.act, a.act_param);
-            x.z = apply_act(x.z, a.act, a.act_param);
-            x.w = apply_act(x.w, a.act, a.act_param);
-            *reinterpret_cast<float4*>(o + 4 * q) = x;
-          }
-        } else {
-          for (int j = 0; j < 16 && col0 + (uint32_t)j < a.n; j++) {
-            float x = v[j];
-            if (ad) x = __fadd_rn(ad[j], x);
-            if (a.bias) x = __fadd_rn(x, a.bias[col0 + j]);
-            o[j] = apply_act(x, a.act, a.act_param);
-          }
+          for (int j = 0; j < 16; j++) acc[c * 16 + j] = __fadd_rn(acc[c * 16 + j], v[j]);
         }
-      }
-      if (nkb > 0) {
         tc_fence_before();
         mbar_arrive(b_acce + 8 * buf);
+        if (++buf == TC_BUFS) {
+          buf = 0;
+          aph ^= 1u;
+        }
       }
-      if (++buf == 2) {
-        buf = 0;
-        aph ^= 1u;
+      if (row >= a.m) continue;
+      float* orow = a.out + (uint64_t)row * a.n;
+      const float* arow = a.addend ? a.addend + (uint64_t)row * a.n : nullptr;
+#pragma unroll
+      for (int c = 0; c < NT / 4; c++) {
+        const uint32_t col = n0 + (uint32_t)c * 4u;
+        if (col >= a.n) break;
+        float x[4] = {acc[4 * c], acc[4 * c + 1], acc[4 * c + 2], acc[4 * c + 3]};
+        if (v4) {
+          if (arow) {
+            const float4 y = *reinterpret_cast<const float4*>(arow + col);
+            x[0] = __fadd_rn(y.x, x[0]);
+            x[1] = __fadd_rn(y.y, x[1]);
+            x[2] = __fadd_rn(y.z, x[2]);
+            x[3] = __fadd_rn(y.w, x[3]);
+          }
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            if (a.bias) x[j] = __fadd_rn(x[j], a.bias[col + j]);
+            x[j] = apply_act(x[j], a.act, a.act_param);
+          }
+          *reinterpret_cast<float4*>(orow + col) = make_float4(x[0], x[1], x[2], x[3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            if (col + (uint32_t)j < a.n) {
+              float y = x[j];
+              if (arow) y = __fadd_rn(arow[col + j], y);
+              if (a.bias) y = __fadd_rn(y, a.bias[col + j]);
+              orow[col + j] = apply_act(y, a.act, a.act_param);
+            }
+          }
+        }
       }
     }
   }
@@ -453,7 +461,9 @@ int bgnn_run_linear_tc(bgnn_ctx* ctx, const float* a1, const float* w1, uint32_t
   auto ok_ptr = [](const void* p) { return ((uintptr_t)p & 15u) == 0; };
   if (k1 % 4 || k2 % 4 || !ok_ptr(a1) || (k2 && !ok_ptr(a2)) || (k1 + k2 == 0))
     return BGNN_ERR_UNSUPPORTED;
-  const int nt = n <= 48 ? (n <= 32 ? 32 : 48) : n <= 64 ? 64 : n <= 128 ? 128 : 256;
+  // tile width: the output width rounded up to 16 (wider outputs take
+  // several 128-column tiles)
+  const int nt = n <= 32 ? 32 : n <= 48 ? 48 : n <= 64 ? 64 : n <= 96 ? 96 : 128;
   // B operands split once per call: [n, k] hi and lo per segment
   DevTmp bsplit;
   const uint64_t b1 = (uint64_t)n * k1, b2 = (uint64_t)n * k2;
@@ -506,7 +516,7 @@ int bgnn_run_linear_tc(bgnn_ctx* ctx, const float* a1, const float* w1, uint32_t
     case 32: return launch_tc<32>(ctx, maps, args);
     case 48: return launch_tc<48>(ctx, maps, args);
     case 64: return launch_tc<64>(ctx, maps, args);
-    case 128: return launch_tc<128>(ctx, maps, args);
-    default: return launch_tc<256>(ctx, maps, args);
+    case 96: return launch_tc<96>(ctx, maps, args);
+    default: return launch_tc<128>(ctx, maps, args);
   }
 }
