@@ -798,7 +798,9 @@ def profile_case(kind, math="fast"):
     gat      : the 2-layer GAT workload (20,000 nodes / 200,000 edges), three
                forwards
     spmm-small: the SpMM on a scale-21 R-MAT matrix (2^25 entries) at F = 32,
-               64, 128, 256."""
+               64, 128, 256
+    giant    : R-MAT scale 20 plus one 4,194,304-edge hub row, F=256 mean
+               aggregation twice (the hub row takes k_agg_giant)."""
     import torch
 
     import browsergnn_b200 as bg
@@ -852,6 +854,30 @@ def profile_case(kind, math="fast"):
             out = l2.forward(l1.forward(g, _act="elu")).x
         torch.cuda.synchronize()
         print(f"GAT forward done, output {tuple(out.shape)}")
+        return
+    if kind == "giant":
+        # R-MAT scale 20 (1,048,576 nodes, 16,777,216 edges) plus one hub row
+        # of 4,194,304 edges, F = 256 mean aggregation, twice: the hub row
+        # takes the giant-row launch (k_agg_giant)
+        scale, n, e0, hub = 20, 1 << 20, 1 << 24, 1 << 22
+        ei = synth.rmat_edges_gpu(scale, n, e0, synth.seed_for(4))
+        gen = torch.Generator("cuda").manual_seed(5)
+        hub_src = torch.randint(0, n, (hub,), device="cuda", generator=gen, dtype=torch.int32)
+        src = torch.cat([ei[:e0], hub_src])
+        dst = torch.cat([ei[e0:], torch.full((hub,), 7, device="cuda", dtype=torch.int32)])
+        e = e0 + hub
+        dg = DeviceGraph(torch.cat([src, dst]), e, n, n)
+        x = torch.randn((n, 256), device="cuda", generator=gen)
+        agg = torch.empty((n, 256), device="cuda")
+        for _ in range(2):
+            a0 = torch.cuda.Event(enable_timing=True)
+            a1 = torch.cuda.Event(enable_timing=True)
+            a0.record()
+            ctx.call("bgnn_aggregate", dg.h, 1, ptr(x), 256, ptr(agg))
+            a1.record()
+            torch.cuda.synchronize()
+            print(f"aggregate mean F=256, {e} edges with a {hub}-edge hub: "
+                  f"{a0.elapsed_time(a1):.3f} ms")
         return
     if kind == "spmm-small":
         # the SpMM sweep on a scale-21 R-MAT matrix (2,097,152 rows, 2^25
@@ -990,7 +1016,7 @@ def main():
     ap.add_argument("--reserve-sms", type=int, default=16,
                     help="N>1: SMs the aggregation leaves to NCCL while chunks are in flight")
     ap.add_argument("--profile", choices=["small", "full-agg", "csr", "csr-small", "linear", "gat",
-                                          "spmm-small"], default=None,
+                                          "spmm-small", "giant"], default=None,
                     help="run one profiling case for ncu and exit")
     args = ap.parse_args()
     if args.profile:
