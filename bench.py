@@ -799,7 +799,7 @@ def profile_case(kind, math="fast"):
                forwards
     spmm-small: the SpMM on a scale-21 R-MAT matrix (2^25 entries) at F = 32,
                64, 128, 256
-    giant    : R-MAT scale 20 plus one 4,194,304-edge hub row, F=256 mean
+    giant    : R-MAT scale 20 plus one 1,048,576-edge hub row, F=256 mean
                aggregation twice (the hub row takes k_agg_giant)."""
     import torch
 
@@ -857,9 +857,9 @@ def profile_case(kind, math="fast"):
         return
     if kind == "giant":
         # R-MAT scale 20 (1,048,576 nodes, 16,777,216 edges) plus one hub row
-        # of 4,194,304 edges, F = 256 mean aggregation, twice: the hub row
+        # of 1,048,576 edges, F = 256 mean aggregation, twice: the hub row
         # takes the giant-row launch (k_agg_giant)
-        scale, n, e0, hub = 20, 1 << 20, 1 << 24, 1 << 22
+        scale, n, e0, hub = 20, 1 << 20, 1 << 24, 1 << 20
         ei = synth.rmat_edges_gpu(scale, n, e0, synth.seed_for(4))
         gen = torch.Generator("cuda").manual_seed(5)
         hub_src = torch.randint(0, n, (hub,), device="cuda", generator=gen, dtype=torch.int32)
