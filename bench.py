@@ -597,10 +597,40 @@ def sage_oracle_parity(ei, n, e, x, weights, got_dev):
         lw = weights[li]
         h = orc.sage_forward_csr(rp, so, n, h, fin, "mean", lw["lin_neighbor"], lw["lin_self"],
                                  lw["bias"], fout, relu=li < 2, threads=0)
-    res = _parity(got, h.reshape(got.shape))
+    want = h.reshape(got.shape)
+    res = _parity(got, want)
     res["checked"] = f"full output [{n}, {WIDTHS[-1]}] of the 3-layer forward"
     res["oracle_seconds"] = round(time.perf_counter() - t0, 1)
-    return res
+    return res, want
+
+
+def tensor_mode_line(ctx, step, steps, warmup, e, want):
+    """The same step with X*W on the tcgen05 tensor cores (3xTF32): time and
+    the count of output elements outside the parity bar against the same
+    oracle output.  Reported beside the headline, which keeps the parity
+    mode."""
+    import torch
+
+    ctx.set_math("tensor")
+    try:
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            step()
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / steps
+        got = step().cpu().numpy()
+    finally:
+        ctx.set_math("fast")
+    return {"ms_per_step": round(ms, 3), "value": 3 * e / (ms * 1e-3), "unit": UNIT,
+            "math": "X*W on tcgen05 (kind::tf32, 3xTF32 split, k-block partials promoted to "
+                    "f32 registers); aggregation unchanged",
+            "parity": _parity(got, want)}
 
 
 # ---------------------------------------------------------------------------
@@ -1185,10 +1215,13 @@ def main():
     # parity at full size: N=1 against the oracle (every output element);
     # N>1 bit for bit against a single-GPU forward of the whole graph, which
     # every rank runs on its own GPU for its own rows
-    parity = None
+    parity = tensor = None
     if not args.no_parity:
         if world == 1:
-            parity = sage_oracle_parity(ei, n, e, x, weights, final)
+            parity, want = sage_oracle_parity(ei, n, e, x, weights, final)
+            if args.math == "fast":
+                tensor = tensor_mode_line(ctx, step, args.steps, args.warmup, e, want)
+            del want
         else:
             parity = partition_bit_identity(ei, n, e, seed, layers, pgd.pg, final, local)
     del final
@@ -1241,6 +1274,8 @@ def main():
             "phase_ms_max_over_ranks": phase_ms,
             "parity": parity,
         }
+        if tensor is not None:
+            line["tensor_mode"] = tensor
         if part_info is not None:
             line["partition"] = part_info
             line["exchange_only_ms_max_over_ranks"] = exchange_only
