@@ -106,6 +106,11 @@ SIGNATURES = {
     "bgnn_prelu": [_P, _P, _U64, _P, _U32, _P],
     "bgnn_link_scores": [_P, _P, _U32, _U32, _P, _P, _U64, _I, _P, _P, _P, _P, _P, _P],
     "bgnn_aggregate_strided": [_P, _P, _I, _P, _P, _U64, _U32, _P, _U64],
+    "bgnn_aggregate_backward": [_P, _P, _I, _P, _P, _U32, _P],
+    "bgnn_gcn_propagate_backward": [_P, _P, _P, _U32, _I, _I, _P],
+    "bgnn_matmul_backward": [_P, _P, _P, _P, _U32, _U32, _U32, _P, _P],
+    "bgnn_bias_backward": [_P, _P, _U64, _U32, _P],
+    "bgnn_relu_backward": [_P, _P, _P, _U64, _P],
     "bgnn_part_create": [_P, _P, _U64, _U32, _U32, _U32, _I, ctypes.POINTER(_P)],
     "bgnn_part_create_csr": [_P, _P, _P, _U32, _U32, _U32, ctypes.POINTER(_P)],
     "bgnn_part_destroy": [_P],

@@ -52,6 +52,7 @@ struct bgnn_graph {
   bool csr_only = false;           // built from an existing CSR (no eid/out_deg)
   float* dinv[2] = {nullptr, nullptr};  // GCN D^-1/2 without / with loop tail
   uint32_t* dst_of = nullptr;      // [E] destination row of each CSR slot (built on first use)
+  bgnn_graph* transpose = nullptr; // rows = sources, edges in COO order (built for the backward)
 };
 
 // Row partition of a square graph / CSR for one rank (partition.cu): rank r
@@ -174,6 +175,9 @@ void bgnn_graph_free(bgnn_graph* g);
 int bgnn_graph_dinv(bgnn_ctx* ctx, bgnn_graph* g, int tail, const float** out);
 int bgnn_graph_dst_of(bgnn_ctx* ctx, bgnn_graph* g, const uint32_t** out);
 int bgnn_graph_dst_of_into(bgnn_ctx* ctx, const bgnn_graph* g, uint32_t* out);
+// the source-keyed transpose of an edge-list graph (backward.cu), built on
+// first use and freed with the graph
+int bgnn_graph_transpose(bgnn_ctx* ctx, bgnn_graph* g, const bgnn_graph** out);
 
 // ---------------------------------------------------------------------------
 // aggregation (aggregate.cu)

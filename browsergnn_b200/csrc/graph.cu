@@ -196,6 +196,10 @@ void bgnn_graph_free(bgnn_graph* g) {
   cudaFree(g->dinv[0]);
   cudaFree(g->dinv[1]);
   cudaFree(g->dst_of);
+  if (g->transpose) {
+    bgnn_graph_free(g->transpose);
+    delete g->transpose;
+  }
   *g = bgnn_graph();
 }
 

@@ -180,6 +180,37 @@ def _linear(ctx, x, w, bias=None, act=None):
     return out
 
 
+def _pre_activation_grad(ctx, grad_out, out, act):
+    """The gradient before the layer's activation (only ReLU is
+    differentiated, as in src/autograd/variable.ts:358-373)."""
+    torch = _torch()
+    if act in (None, "none"):
+        return grad_out.contiguous()
+    if act != "relu":
+        raise NotImplementedError(f"backward through activation {act!r}")
+    g = torch.empty_like(grad_out)
+    ctx.call("bgnn_relu_backward", ptr(grad_out.contiguous()), ptr(out), out.numel(), ptr(g))
+    return g
+
+
+def _matmul_backward(ctx, a, w, g):
+    """(grad_a, grad_w) of a @ w (Variable.matmul, variable.ts:213-235)."""
+    torch = _torch()
+    m, k = a.shape
+    n = w.shape[1]
+    ga = torch.empty((m, k), dtype=torch.float32, device=a.device)
+    gw = torch.empty((k, n), dtype=torch.float32, device=a.device)
+    ctx.call("bgnn_matmul_backward", ptr(a), ptr(w), ptr(g), m, k, n, ptr(ga), ptr(gw))
+    return ga, gw
+
+
+def _bias_backward(ctx, g):
+    torch = _torch()
+    out = torch.empty(g.shape[1], dtype=torch.float32, device=g.device)
+    ctx.call("bgnn_bias_backward", ptr(g), g.shape[0], g.shape[1], ptr(out))
+    return out
+
+
 class GCNConv(Module):
     """src/layers/gcn.ts:34-286."""
 
@@ -209,6 +240,28 @@ class GCNConv(Module):
         return input.withFeatures(out)
 
     forwardAsync = forward
+
+    def backward(self, input: GraphData, grad_out, _act=None, output=None) -> dict:
+        """Gradients of forward(input, _act) for an upstream gradient
+        grad_out [N, out]: {"x", "weight", "bias"}.  The reference never
+        differentiates a layer; this is the adjoint of each forward step
+        (bgnn_gcn_propagate_backward for the propagation, Variable.matmul's
+        backward for X @ W, the broadcast reduction for the bias, ReLU's
+        mask).  `output` is the forward's output (recomputed when omitted)."""
+        dg, x = _prepare(self, input, self.inChannels, "GCNConv")
+        ctx = dg.ctx
+        torch = _torch()
+        if _act not in (None, "none") and output is None:
+            output = self.forward(input, _act=_act).x
+        g = _pre_activation_grad(ctx, grad_out, output, _act)
+        grads = {}
+        if self.useBias:
+            grads["bias"] = _bias_backward(ctx, g)
+        gh = torch.empty_like(g)
+        ctx.call("bgnn_gcn_propagate_backward", dg.h, ptr(g), self.outChannels,
+                 int(self.addSelfLoops), int(self.normalize), ptr(gh))
+        grads["x"], grads["weight"] = _matmul_backward(ctx, x, self.p("weight"), gh)
+        return grads
 
     def __repr__(self):
         return (f"GCNConv({self.inChannels} -> {self.outChannels}, bias={self.useBias}, "
@@ -333,6 +386,36 @@ class SAGEConv(Module):
         return input.withFeatures(out)
 
     forwardAsync = forward
+
+    def backward(self, input: GraphData, grad_out, _act=None, output=None) -> dict:
+        """Gradients of forward(input, _act) for an upstream gradient
+        grad_out [N, out]: {"x", "lin_neighbor", "lin_self", "bias"} (sum,
+        mean and max aggregators, no L2 normalisation).  Each forward step's
+        adjoint: ReLU's mask, the broadcast bias reduction, Variable.matmul's
+        backward for both products (variable.ts:213-235), and the message
+        passing's edge-ordered scatter over the sources
+        (bgnn_aggregate_backward); grad x = f32(x-path + message-path)."""
+        if self.aggregator == "pool" or self.normalize:
+            raise NotImplementedError("backward of the pool aggregator / L2 normalisation")
+        torch = _torch()
+        dg, x = _prepare(self, input, self.inChannels, "SAGEConv")
+        ctx = dg.ctx
+        if _act not in (None, "none") and output is None:
+            output = self.forward(input, _act=_act).x
+        g = _pre_activation_grad(ctx, grad_out, output, _act)
+        agg = self.aggregate(dg, x)
+        grads = {}
+        if self.useBias:
+            grads["bias"] = _bias_backward(ctx, g)
+        gagg, grads["lin_neighbor"] = _matmul_backward(ctx, agg, self.p("lin_neighbor"), g)
+        gx = torch.empty_like(x)
+        ctx.call("bgnn_aggregate_backward", dg.h, _lib.AGGR[self.aggregator], ptr(x), ptr(gagg),
+                 self.inChannels, ptr(gx))
+        if self.rootWeight:
+            gself, grads["lin_self"] = _matmul_backward(ctx, x, self.p("lin_self"), g)
+            ctx.call("bgnn_add_dev", ptr(gself), ptr(gx), gx.numel(), ptr(gx))
+        grads["x"] = gx
+        return grads
 
 
 class GINConv(Module):

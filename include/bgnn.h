@@ -302,6 +302,44 @@ BGNN_API int bgnn_segment_sum(bgnn_ctx* ctx, const float* x, uint32_t num_featur
 BGNN_API int bgnn_pack_rows(bgnn_ctx* ctx, const float* x, uint32_t num_x_rows, const uint32_t* rows,
                    uint32_t num_rows, uint32_t num_features, float* out);
 
+/* ---- backward ----------------------------------------------------------
+ * The reference's autograd differentiates X*W (Variable.matmul,
+ * src/autograd/variable.ts:213-235), ReLU (variable.ts:358-373) and the
+ * broadcast bias add (variable.ts:665-688) but not the message passing.  The
+ * message-passing gradients below are the adjoint of the forward as that
+ * autograd would compute it if gather and scatter were autograd ops: edge e
+ * carries a message from grad[dst(e)], scatter-added over the sources in COO
+ * edge order with an f32 store after every add (wasmScatterAdd,
+ * src/backend/wasm/index.ts:70-105).  They run on the graph's transpose,
+ * built on first use and kept with the graph (graphs from an edge list). */
+/* grad_x [N_src, F] of bgnn_aggregate: sum: m_e = grad[dst]; mean:
+ * m_e = f32(grad[dst] * (1/cnt(dst))), 1/cnt in double; max: m_e = grad[dst]
+ * for the edge that last raised the forward maximum of that feature (x > acc
+ * in edge order from -inf; x = the forward input), else 0. */
+BGNN_API int bgnn_aggregate_backward(bgnn_ctx* ctx, const bgnn_graph* g, int aggr,
+                                     const float* x, const float* grad, uint32_t num_features,
+                                     float* grad_x);
+/* grad_h [N, F] of bgnn_gcn_propagate before its bias and activation:
+ * m_e = f32(grad[dst] * w_e) with the forward's norm w_e, the appended
+ * self-loop edges (when the forward appended them) last. */
+BGNN_API int bgnn_gcn_propagate_backward(bgnn_ctx* ctx, const bgnn_graph* g, const float* grad,
+                                         uint32_t num_features, int add_self_loops,
+                                         int normalize, float* grad_h);
+/* Variable.matmul backward (variable.ts:213-235), out = a[m,k] * b[k,n]:
+ * grad_a [m, k] = grad @ transpose(b), grad_b [k, n] = transpose(a) @ grad,
+ * each output one k-ascending chain as wasmMatmul computes it (either may be
+ * NULL). */
+BGNN_API int bgnn_matmul_backward(bgnn_ctx* ctx, const float* a, const float* b,
+                                  const float* grad, uint32_t m, uint32_t k, uint32_t n,
+                                  float* grad_a, float* grad_b);
+/* The bias gradient of a broadcast add (variable.ts:675-685): out[j] = the
+ * row-ordered f32 sum of grad[:, j]. */
+BGNN_API int bgnn_bias_backward(bgnn_ctx* ctx, const float* grad, uint64_t rows, uint32_t cols,
+                                float* out);
+/* ReLU backward (variable.ts:358-373): grad where the forward output > 0. */
+BGNN_API int bgnn_relu_backward(bgnn_ctx* ctx, const float* grad, const float* out, uint64_t n,
+                                float* grad_in);
+
 /* ---- row partition of a graph across the GPUs of one node ---------------
  * No counterpart in the reference, which is single-device: these run the
  * message passing of SAGEConv.forward (src/layers/sage.ts:113-217) and

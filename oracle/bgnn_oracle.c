@@ -681,6 +681,123 @@ int orc_sage_forward_csr(const uint32_t* row_ptr, const uint32_t* src_of, int64_
   return 0;
 }
 
+/* ---- backward of the message passing and of X*W ------------------------
+ * The reference's autograd (src/autograd/variable.ts) has a matmul backward
+ * (variable.ts:213-235: gradA = grad @ B^T, gradB = A^T @ grad through
+ * Tensor.transpose and wasmMatmul) and a broadcast bias reduction
+ * (variable.ts:665-688), but never differentiates through MessagePassing.
+ * The message-passing adjoint below is what it would compute if its
+ * gather / scatter were autograd ops: edge e carries a message m_e derived
+ * from grad[dst(e)], and the messages are scatter-added over the sources in
+ * COO edge order (wasmScatterAdd, src/backend/wasm/index.ts:70-105):
+ *   op 0 sum   m_e = grad[dst]
+ *   op 1 mean  m_e = f32(grad[dst] * (1 / cnt(dst))), 1/cnt in double
+ *   op 2 max   m_e = grad[dst] where src(e) supplied the forward maximum of
+ *              that feature (the edge that last raised it: x > acc in COO
+ *              order from -inf), else 0
+ *   op 3 gcn   m_e = f32(grad[dst] * w_e), w_e the computeGCNNorm weight;
+ *              tail != 0 appends the self-loop edges (i, i) after the edges
+ * out [n, f] (zeros first). */
+void orc_aggregate_backward(const uint32_t* ei, int64_t e, int64_t n, const float* x,
+                            const float* grad, int64_t f, int op, int tail, float* out) {
+  const uint32_t* src = ei;
+  const uint32_t* dst = ei + e;
+  for (int64_t i = 0; i < n * f; i++) out[i] = 0.0f;
+  int64_t* arg = NULL;
+  uint32_t* cnt = NULL;
+  float* dinv = NULL;
+  if (op == 2) {
+    float* acc = (float*)malloc(sizeof(float) * (size_t)(n * f + 1));
+    arg = (int64_t*)malloc(sizeof(int64_t) * (size_t)(n * f + 1));
+    for (int64_t i = 0; i < n * f; i++) {
+      acc[i] = -INFINITY;
+      arg[i] = -1;
+    }
+    for (int64_t q = 0; q < e; q++) {
+      const float* xs = x + (int64_t)src[q] * f;
+      float* a = acc + (int64_t)dst[q] * f;
+      int64_t* g = arg + (int64_t)dst[q] * f;
+      for (int64_t j = 0; j < f; j++)
+        if (xs[j] > a[j]) {
+          a[j] = xs[j];
+          g[j] = q;
+        }
+    }
+    free(acc);
+  } else if (op == 1) {
+    cnt = (uint32_t*)calloc((size_t)n + 1, sizeof(uint32_t));
+    for (int64_t q = 0; q < e; q++) cnt[dst[q]]++;
+  } else if (op == 3) {
+    dinv = (float*)malloc(sizeof(float) * (size_t)(n + 1));
+    gcn_dinv(ei, e, n, tail, dinv);
+  }
+  const int64_t total = e + ((op == 3 && tail) ? n : 0);
+  for (int64_t q = 0; q < total; q++) {
+    const int64_t s = q < e ? (int64_t)src[q] : q - e;
+    const int64_t d = q < e ? (int64_t)dst[q] : q - e;
+    const float* gd = grad + d * f;
+    float* o = out + s * f;
+    if (op == 0) {
+      for (int64_t j = 0; j < f; j++) o[j] = (float)((double)o[j] + (double)gd[j]);
+    } else if (op == 1) {
+      const double inv = 1.0 / (double)cnt[d];
+      for (int64_t j = 0; j < f; j++) {
+        const float m = (float)((double)gd[j] * inv);
+        o[j] = (float)((double)o[j] + (double)m);
+      }
+    } else if (op == 2) {
+      const int64_t* g = arg + d * f;
+      for (int64_t j = 0; j < f; j++) {
+        const float m = g[j] == q ? gd[j] : 0.0f;
+        o[j] = (float)((double)o[j] + (double)m);
+      }
+    } else {
+      const double w = (double)(float)((double)dinv[s] * (double)dinv[d]);
+      for (int64_t j = 0; j < f; j++) {
+        const float m = (float)((double)gd[j] * w);
+        o[j] = (float)((double)o[j] + (double)m);
+      }
+    }
+  }
+  free(arg);
+  free(cnt);
+  free(dinv);
+}
+
+/* Tensor.transpose, src/core/tensor.ts:131-144 */
+static float* transpose_new(const float* a, int64_t rows, int64_t cols) {
+  float* t = (float*)malloc(sizeof(float) * (size_t)(rows * cols + 1));
+  for (int64_t i = 0; i < rows; i++)
+    for (int64_t j = 0; j < cols; j++) t[j * rows + i] = a[i * cols + j];
+  return t;
+}
+
+/* Variable.matmul backward, src/autograd/variable.ts:213-235:
+ * grad_a [m, k] = grad [m, n] @ transpose(b); grad_b [k, n] = transpose(a) @ grad.
+ * Either output may be NULL. */
+void orc_matmul_backward(const float* a, const float* b, const float* grad, int64_t m, int64_t k,
+                         int64_t n, float* grad_a, float* grad_b) {
+  if (grad_a) {
+    float* bt = transpose_new(b, k, n);
+    orc_matmul(grad, bt, m, n, k, grad_a);
+    free(bt);
+  }
+  if (grad_b) {
+    float* at = transpose_new(a, m, k);
+    orc_matmul(at, grad, k, m, n, grad_b);
+    free(at);
+  }
+}
+
+/* The bias gradient of a broadcast add, Variable._reduceBroadcast
+ * (src/autograd/variable.ts:675-685): out[j] = sum over rows, in row order,
+ * stored to a Float32Array after every step. */
+void orc_bias_backward(const float* grad, int64_t rows, int64_t cols, float* out) {
+  for (int64_t j = 0; j < cols; j++) out[j] = 0.0f;
+  for (int64_t i = 0; i < rows; i++)
+    for (int64_t j = 0; j < cols; j++) out[j] = (float)((double)out[j] + (double)grad[i * cols + j]);
+}
+
 /* ======================================================================= */
 /* model zoo                                                               */
 /* ======================================================================= */

@@ -123,6 +123,17 @@ void orc_spmm_rows(const uint32_t* row_ptr, const uint32_t* col, const float* va
                    const float* dense, int64_t nf, const uint32_t* rows, int64_t nrows,
                    int threads, float* out);
 
+/* ---- backward (no reference counterpart for the message passing; the
+ *      matmul backward and bias reduction follow src/autograd/variable.ts) */
+/* op: 0 sum, 1 mean, 2 max (x = the forward's input), 3 gcn (tail: appended
+ * self-loops); out [n, f] = the gradient for the source rows. */
+void orc_aggregate_backward(const uint32_t* edge_index, int64_t num_edges, int64_t num_nodes,
+                            const float* x, const float* grad, int64_t f, int op, int tail,
+                            float* out);
+void orc_matmul_backward(const float* a, const float* b, const float* grad, int64_t m, int64_t k,
+                         int64_t n, float* grad_a, float* grad_b);
+void orc_bias_backward(const float* grad, int64_t rows, int64_t cols, float* out);
+
 /* ---- model zoo: src/nn/linear.ts, src/nn/activation.ts, src/core/tensor.ts,
  *      and the three models under src/models/ ------------------------------ */
 /* Linear.forward (src/nn/linear.ts:50-111): y[r,j] = f32(sum_i x[r,i]*w[j,i])

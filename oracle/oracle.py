@@ -56,6 +56,10 @@ def _declare(L):
         "orc_spmv": (v, [_U, _U, _F, _F, _I64, _F]),
         "orc_spmm": (v, [_U, _U, _F, _F, _I64, _I64, _F]),
         "orc_spmm_rows": (v, [_U, _U, _F, _F, _I64, _U, _I64, ctypes.c_int, _F]),
+        "orc_aggregate_backward": (v, [_U, _I64, _I64, _F, _F, _I64, ctypes.c_int, ctypes.c_int,
+                                       _F]),
+        "orc_matmul_backward": (v, [_F, _F, _F, _I64, _I64, _I64, _F, _F]),
+        "orc_bias_backward": (v, [_F, _I64, _I64, _F]),
         "orc_coo_spmm": (v, [_U, _U, _F, _I64, _I64, _F, _I64, _F]),
         "orc_coo_to_csr": (ctypes.c_int, [_U, _U, _F, _I64, _I64, _U, _U, _F]),
         "orc_gcn_norm": (v, [_U, _I64, _I64, ctypes.c_int, _F]),
@@ -367,6 +371,35 @@ def sage_forward_csr(row_ptr, src_of, n, x, fin, aggr, lin_neighbor, lin_self, b
                                     SAGE_AGGR[aggr], _pf(_f(lin_neighbor)), _pf(_f(lin_self)),
                                     _pf(_f(bias)), fout, int(relu), threads, _pf(out))
     assert rc == 0
+    return out
+
+
+# ---- backward --------------------------------------------------------------
+BACKWARD_OPS = {"sum": 0, "mean": 1, "max": 2, "gcn": 3}
+
+
+def aggregate_backward(edge_index, num_edges, num_nodes, grad, f, op, x=None, tail=False):
+    """Gradient for the source rows of sum / mean / max / gcn aggregation
+    (the edge-ordered scatter of gradient messages); x is the forward input
+    (needed for max)."""
+    out = np.empty(num_nodes * f, np.float32)
+    xx = _f(x) if x is not None else np.zeros(1, np.float32)
+    lib().orc_aggregate_backward(_pu(_u(edge_index)), num_edges, num_nodes, _pf(xx),
+                                 _pf(_f(grad)), f, BACKWARD_OPS[op], int(tail), _pf(out))
+    return out
+
+
+def matmul_backward(a, b, grad, m, k, n):
+    """(grad_a [m, k], grad_b [k, n]) of Variable.matmul (variable.ts:213-235)."""
+    ga = np.empty(m * k, np.float32)
+    gb = np.empty(k * n, np.float32)
+    lib().orc_matmul_backward(_pf(_f(a)), _pf(_f(b)), _pf(_f(grad)), m, k, n, _pf(ga), _pf(gb))
+    return ga, gb
+
+
+def bias_backward(grad, rows, cols):
+    out = np.empty(cols, np.float32)
+    lib().orc_bias_backward(_pf(_f(grad)), rows, cols, _pf(out))
     return out
 
 

@@ -122,3 +122,59 @@ def test_spmm_rows_matches_sequential_spmm():
     pick = np.array([7, 0, 299, 150], np.uint32)
     sub = orc.spmm_rows(rp, ci, va, x, f, rows=pick, threads=2).reshape(-1, f)
     assert np.array_equal(sub.view(np.uint32), want[pick].view(np.uint32))
+
+
+def test_backward_restatement_is_gather_then_edge_ordered_scatter():
+    # The message-passing adjoint equals wasmGather of the gradient rows by
+    # destination, a per-edge message, then wasmScatterAdd over the sources
+    # (both pinned by the reference's KATs above).
+    rng = np.random.default_rng(5)
+    n, e, f = 40, 300, 3
+    src = rng.integers(0, n, e).astype(np.uint32)
+    dst = rng.integers(0, n, e).astype(np.uint32)
+    ei = np.concatenate([src, dst])
+    g = rng.standard_normal((n, f)).astype(np.float32)
+    x = rng.standard_normal((n, f)).astype(np.float32)
+    gathered = orc.gather(g, dst, f).reshape(e, f)
+    want = orc.scatter_add(gathered, src, n, f)
+    got = orc.aggregate_backward(ei, e, n, g, f, "sum")
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    cnt = np.bincount(dst, minlength=n).astype(np.float64)
+    msgs = (gathered.astype(np.float64) * (1.0 / cnt[dst])[:, None]).astype(np.float32)
+    want = orc.scatter_add(msgs, src, n, f)
+    got = orc.aggregate_backward(ei, e, n, g, f, "mean")
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    w = orc.gcn_norm(ei, e, n, False).astype(np.float64)
+    msgs = (gathered.astype(np.float64) * w[:, None]).astype(np.float32)
+    want = orc.scatter_add(msgs, src, n, f)
+    got = orc.aggregate_backward(ei, e, n, g, f, "gcn")
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    # max: each (dst, feature) routes its gradient to the edge that last
+    # raised the running maximum (x > acc in COO order)
+    arg = -np.ones((n, f), np.int64)
+    acc = np.full((n, f), -np.inf, np.float32)
+    for q in range(e):
+        up = x[src[q]] > acc[dst[q]]
+        acc[dst[q]][up] = x[src[q]][up]
+        arg[dst[q]][up] = q
+    msgs = np.where(arg[dst] == np.arange(e)[:, None], gathered, 0.0).astype(np.float32)
+    want = orc.scatter_add(msgs, src, n, f)
+    got = orc.aggregate_backward(ei, e, n, g, f, "max", x=x)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_matmul_backward_restatement():
+    # variable.ts:213-235: grad @ B^T and A^T @ grad through Tensor.transpose
+    rng = np.random.default_rng(6)
+    m, k, n = 7, 5, 4
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b = rng.standard_normal((k, n)).astype(np.float32)
+    g = rng.standard_normal((m, n)).astype(np.float32)
+    ga, gb = orc.matmul_backward(a, b, g, m, k, n)
+    assert np.array_equal(ga, orc.matmul(g, np.ascontiguousarray(b.T), m, n, k))
+    assert np.array_equal(gb, orc.matmul(np.ascontiguousarray(a.T), g, k, m, n))
+    bias = orc.bias_backward(g, m, n)
+    want = np.zeros(n, np.float32)
+    for i in range(m):
+        want = (want.astype(np.float64) + g[i]).astype(np.float32)
+    assert np.array_equal(bias, want)
