@@ -21,7 +21,7 @@ host-side mirror of the reference's API for that path:
 from ._lib import BGNNError, BGNNIndexError
 from .backend import (CudaComputeManager, get_backend, get_compute_manager, get_context,
                       getBackend, getComputeManager, init_browsergnn, initBrowserGNN,
-                      is_gpu_available, isGPUAvailable)
+                      is_gpu_available, isGPUAvailable, to_host)
 from .graph import DeviceGraph, GraphData, batch_graphs, batchGraphs, from_edge_list, fromEdgeList
 from .layers import (ELU, GATConv, GCNConv, GINConv, LeakyReLU, Module, ReLU, SAGEConv,
                      Sequential, global_sum_pool)
@@ -41,6 +41,7 @@ __all__ = [
     "Module", "ReLU", "SAGEConv", "Sequential", "SparseCOO", "SparseCSR", "batchGraphs",
     "batch_graphs", "computeGCNNorm", "compute_gcn_norm", "fromEdgeList", "from_edge_list",
     "getBackend", "getComputeManager", "get_backend", "get_compute_manager", "get_context",
+    "to_host",
     "global_sum_pool", "initBrowserGNN", "init_browsergnn", "isGPUAvailable", "is_gpu_available",
     "Linear", "Sigmoid", "Tanh", "GELU", "SiLU", "PReLU", "Softmax", "LogSoftmax", "Dropout",
     "manual_seed", "StudentMasteryPredictor", "LearningPathRecommender",

@@ -58,6 +58,8 @@ SIGNATURES = {
     "bgnn_ctx_synchronize": [_P],
     "bgnn_last_error": [_P],
     "bgnn_ctx_launch_count": [_P],
+    "bgnn_memcpy_h2d": [_P, _P, _P, _U64],
+    "bgnn_memcpy_d2h": [_P, _P, _P, _U64],
     "bgnn_spmm_host": [_P, _P, _P, _P, _P, _U32, _U32, _U32, _P],
     "bgnn_scatter_add_host": [_P, _P, _P, _U64, _U32, _U32, _P],
     "bgnn_scatter_mean_host": [_P, _P, _P, _U64, _U32, _U32, _P],

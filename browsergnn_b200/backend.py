@@ -116,16 +116,35 @@ def ptr(t) -> Optional[int]:
 
 
 def as_device(a, dtype, device: int):
-    """numpy / list / torch -> contiguous CUDA tensor of `dtype`."""
+    """numpy / list / torch -> contiguous CUDA tensor of `dtype`.  Host
+    arrays go through the library's staged copy (bgnn_memcpy_h2d)."""
     torch = _torch()
     if isinstance(a, torch.Tensor):
         t = a.to(device=f"cuda:{device}", dtype=dtype)
         return t.contiguous()
     npdt = {torch.float32: np.float32, torch.int32: np.uint32}[dtype]
     arr = np.ascontiguousarray(np.asarray(a, dtype=npdt))
-    if npdt is np.uint32:
-        arr = arr.view(np.int32)
-    return torch.from_numpy(arr).to(f"cuda:{device}")
+    t = torch.empty(arr.shape, dtype=dtype, device=f"cuda:{device}")
+    if arr.size:
+        get_context(device).call("bgnn_memcpy_h2d", ptr(t), arr.ctypes.data, arr.nbytes)
+    return t
+
+
+def to_host(t, out: Optional[np.ndarray] = None) -> np.ndarray:
+    """A CUDA tensor's values in a host float32 / uint32 array (a fresh one, as
+    WebGPUComputeManager returns, or `out`), through the library's staged
+    copy (bgnn_memcpy_d2h): no page-locked memory needed on the caller's
+    side."""
+    torch = _torch()
+    t = t.contiguous()
+    npdt = {torch.float32: np.float32, torch.int32: np.uint32}[t.dtype]
+    if out is None:
+        out = np.empty(tuple(t.shape), npdt)
+    if out.nbytes != t.numel() * t.element_size() or not out.flags.c_contiguous:
+        raise ValueError("out must be a contiguous array of the tensor's size")
+    if out.size:
+        get_context(t.device.index).call("bgnn_memcpy_d2h", out.ctypes.data, ptr(t), out.nbytes)
+    return out
 
 
 # ---- backend manager mirror ---------------------------------------------------

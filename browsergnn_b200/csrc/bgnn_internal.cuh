@@ -158,6 +158,10 @@ int bgnn_radix_sort(bgnn_ctx* ctx, const uint32_t* keys_in, uint64_t n, int key_
                     uint32_t* p0_out, uint32_t* p1_out);
 int bgnn_bits_for(uint64_t max_value);
 int bgnn_iota(bgnn_ctx* ctx, uint32_t* out, uint64_t n);
+// synchronous copies of caller host memory (hostcopy.cu): page-locked memory
+// directly, pageable memory staged through library-owned pinned chunks
+int bgnn_copy_h2d(bgnn_ctx* ctx, void* dst, const void* src, uint64_t bytes);
+int bgnn_copy_d2h(bgnn_ctx* ctx, void* dst, const void* src, uint64_t bytes);
 int bgnn_check_device_error(bgnn_ctx* ctx);
 
 // ---------------------------------------------------------------------------

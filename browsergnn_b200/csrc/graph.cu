@@ -361,14 +361,10 @@ extern "C" int bgnn_graph_create(bgnn_ctx* ctx, const uint32_t* edge_index, uint
   const uint32_t* ei = edge_index;
   int rc = BGNN_OK;
   if (on_host && num_edges) {
+    // pageable host memory is staged through the library's pinned chunks
     rc = bgnn_tmp_alloc(ctx, staged, num_edges * 8);
-    if (rc == BGNN_OK) {
-      cudaError_t e = cudaMemcpyAsync(staged.p, edge_index, num_edges * 8, cudaMemcpyHostToDevice,
-                                      ctx->stream);
-      if (e != cudaSuccess) rc = bgnn_set_error(ctx, BGNN_ERR_CUDA, "H2D copy failed: %s",
-                                                cudaGetErrorString(e));
-      ei = staged.as<uint32_t>();
-    }
+    if (rc == BGNN_OK) rc = bgnn_copy_h2d(ctx, staged.p, edge_index, num_edges * 8);
+    ei = staged.as<uint32_t>();
   }
   if (rc == BGNN_OK) rc = bgnn_graph_build(ctx, ei, ei + num_edges, num_edges, num_src, num_dst, g);
   if (rc == BGNN_OK) {

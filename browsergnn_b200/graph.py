@@ -134,6 +134,8 @@ class GraphData:
             raise ValueError(
                 f"Node features length {xlen} doesn't match numNodes({n}) * numFeatures({f})")
         self.x = x.reshape(n, f)
+        self._x_dev = None       # device copy of a host x (made once)
+        self._x_upload = None    # (thread, tensor, status) of an upload in flight
         self.numNodes = n
         self.numFeatures = f
         if _is_cuda_tensor(ei):
@@ -152,9 +154,15 @@ class GraphData:
             arr = arr.reshape(-1)
             if arr.size != 2 * e:
                 raise ValueError(f"Edge index length {arr.size} doesn't match numEdges({e}) * 2")
-            # graph.ts:88-92: the first out-of-range entry in flat order
-            if arr.size and (int(arr.max()) >= n or (arr.dtype.kind == "i" and int(arr.min()) < 0)):
-                bad = np.flatnonzero((arr >= n) | (arr < 0))
+            # graph.ts:88-92: the first out-of-range entry in flat order.  Large
+            # unsigned lists are checked by the device CSR build instead (the
+            # same error, found in the same pass that counts the degrees).
+            if arr.dtype.kind == "i" and arr.size and int(arr.min()) < 0:
+                bad = np.flatnonzero(arr < 0)
+                raise ValueError(f"Edge index {arr[bad[0]]} out of bounds for {n} nodes")
+            if arr.size and (arr.size <= _HOST_CHECK_MAX or not _device_present()) and \
+                    int(arr.max()) >= n:
+                bad = np.flatnonzero(arr >= n)
                 raise ValueError(f"Edge index {arr[bad[0]]} out of bounds for {n} nodes")
             self.edgeIndex = np.ascontiguousarray(arr, dtype=np.uint32)
             self.numEdges = e
@@ -168,9 +176,34 @@ class GraphData:
     # ---- device structure ----
     def device_graph(self, device: Optional[int] = None) -> DeviceGraph:
         if self._dgraph is None:
+            # a host x starts uploading now, beside the CSR build
+            self._start_x_upload(device)
             self._dgraph = DeviceGraph(self.edgeIndex, self.numEdges, self.numNodes, self.numNodes,
                                        device=device)
         return self._dgraph
+
+    def _start_x_upload(self, device: Optional[int]):
+        """Upload a host x on a second host thread (the library's staged copy
+        releases the interpreter while it runs), so that it overlaps the
+        edge list's upload and the CSR build; x_device() waits for it."""
+        if not isinstance(self.x, np.ndarray) or self._x_dev is not None or \
+                self._x_upload is not None or self.x.size == 0:
+            return
+        import threading
+
+        torch = _torch()
+        ctx = get_context(device)
+        arr = np.ascontiguousarray(self.x, dtype=np.float32)
+        t = torch.empty(arr.shape, dtype=torch.float32, device=f"cuda:{ctx.device}")
+        status = [None]
+        ctx.bind()
+
+        def run():
+            status[0] = ctx.lib.bgnn_memcpy_h2d(ctx.h, ptr(t), arr.ctypes.data, arr.nbytes)
+
+        th = threading.Thread(target=run, daemon=True)
+        th.start()
+        self._x_upload = (th, t, status, arr)
 
     def x_device(self, device: Optional[int] = None):
         torch = _torch()
@@ -178,8 +211,28 @@ class GraphData:
             torch.cuda.current_stream().wait_event(self._x_ready)
         if _is_cuda_tensor(self.x) and self.x.dtype == torch.float32:
             return self.x.contiguous()
-        dev = self.device_graph(device).device
-        return as_device(self.x, torch.float32, dev).reshape(self.numNodes, self.numFeatures)
+        if self._x_dev is not None:
+            return self._x_dev
+        dev = self.device_graph(device).device  # may start the upload
+        if self._x_upload is not None:
+            th, t, status, _ = self._x_upload
+            th.join()
+            self._x_upload = None
+            _lib.check(status[0], get_context(t.device.index).h)
+            self._x_dev = t.reshape(self.numNodes, self.numFeatures)
+        else:
+            self._x_dev = as_device(self.x, torch.float32, dev).reshape(self.numNodes,
+                                                                        self.numFeatures)
+        return self._x_dev
+
+    def x_host(self) -> np.ndarray:
+        """x as a host float32 array (a layer's output read back through the
+        library's staged copy)."""
+        if isinstance(self.x, np.ndarray):
+            return self.x
+        from .backend import to_host
+
+        return to_host(self.x)
 
     # ---- reference helpers (graph.ts:135-325) ----
     def _host_edges(self) -> np.ndarray:
@@ -253,8 +306,20 @@ class GraphData:
         g.__dict__.update(self.__dict__)
         g.x = new_x
         g._x_ready = None
+        g._x_dev = None
+        g._x_upload = None
         g.numFeatures = int(new_x.shape[1])
         return g
+
+
+_HOST_CHECK_MAX = 1 << 20  # edge-list entries checked on the host when a GPU is present
+
+
+def _device_present() -> bool:
+    try:
+        return _torch().cuda.is_available()
+    except Exception:  # pragma: no cover
+        return False
 
 
 def _is_pinned_host(a) -> bool:

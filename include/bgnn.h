@@ -117,6 +117,17 @@ BGNN_API const char* bgnn_last_error(const bgnn_ctx* ctx);
 /* Count of this library's kernel launches on the context (for accounting). */
 BGNN_API uint64_t bgnn_ctx_launch_count(const bgnn_ctx* ctx);
 
+/* Copies between caller host memory and device memory, returning when the
+ * data is in place (the reference uploads each operand from a typed array
+ * and reads a fresh one back, compute-pipeline.ts:182-190).  They first wait
+ * for the work already queued on the context's stream.  Page-locked host
+ * memory is copied directly; pageable memory (JS typed arrays, numpy) is
+ * staged through pinned chunks the library owns, each filled or drained by a
+ * pool of host threads while the DMA of the next chunk runs.  Safe to call
+ * from two host threads at once (two staging rings per device). */
+BGNN_API int bgnn_memcpy_h2d(bgnn_ctx* ctx, void* dst_dev, const void* src_host, uint64_t bytes);
+BGNN_API int bgnn_memcpy_d2h(bgnn_ctx* ctx, void* dst_host, const void* src_dev, uint64_t bytes);
+
 /* ---- facade mirror: WebGPUComputeManager methods, host buffers ---------- */
 /* spmm: compute-pipeline.ts:140-232 / wasmSpmm index.ts:342-383 */
 BGNN_API int bgnn_spmm_host(bgnn_ctx* ctx, const uint32_t* row_ptr, const uint32_t* col_indices,
