@@ -6,13 +6,13 @@
 // (src/core/sparse.ts:322-344) on a partitioned graph with the same per-row
 // order and roundings as on one GPU, so the result is the same bits.
 //
-// Pipelining: a layer's features are exchanged in column chunks on a
-// high-priority stream, and the aggregation of chunk c (its columns of every
-// row, each row still summed in edge order) starts as soon as chunk c has
-// landed, while later chunks are still in flight.  The persistent
-// aggregation then leaves `reserve` SMs to the NCCL kernels.  The root-weight
-// product x * W_self needs only owned rows and runs on a side stream from the
-// start of the layer.
+// Overlap: the halo exchange starts on a high-priority stream at the start of
+// the layer, while the root-weight product x * W_self (owned rows only) runs
+// on a side stream; the aggregation starts when the halo rows have landed.
+// On request (bgnn_dist_set_pipeline) the exchange runs in column chunks and
+// the aggregation of chunk c (its columns of every row, each row still summed
+// in edge order) starts as soon as chunk c has landed, leaving `reserve` SMs
+// to the NCCL kernels while later chunks are in flight.
 //
 // Timeouts: the communicator is created non-blocking and every piece of NCCL
 // work is watched by a thread that aborts the communicator when the work is
@@ -248,9 +248,14 @@ struct GridBudget {
   ~GridBudget() { ctx->grid_sms = saved; }
 };
 
+// One chunk unless the caller asks for more: a column slice re-walks every
+// edge's index and row bookkeeping, so four 64-column aggregations of a
+// 256-column layer took 6.67 ms against 4.68 ms for one (2 GPUs), more than
+// the 1.2 ms exchange they would hide -- which x * W_self already covers
+// (2-GPU step 26.4 ms with one chunk, 31.4 ms with four).
 uint32_t pick_chunks(const bgnn_dist* d, uint32_t f) {
   if (d->world == 1) return 1;
-  uint32_t c = d->chunks ? d->chunks : (f >= 192 ? 4 : (f >= 96 ? 2 : 1));
+  uint32_t c = d->chunks ? d->chunks : 1u;
   if (c > kMaxChunks) c = kMaxChunks;
   while (c > 1 && f / c < 8) c--;
   return c;

@@ -427,17 +427,18 @@ BGNN_API int bgnn_dist_destroy(bgnn_dist* d);
  * gone): pending NCCL work ends, later calls return BGNN_ERR_DEVICE, and
  * bgnn_dist_destroy then needs no peer. */
 BGNN_API int bgnn_dist_abort(bgnn_dist* d);
-/* column chunks of the pipelined exchange (0: by width, 4 at >= 192 columns,
- * 2 at >= 96, else 1) and SMs left to NCCL while later chunks fly */
+/* column chunks of the exchange (0 or 1: one; a column slice re-walks every
+ * edge, so more chunks pay only when the exchange outlasts x*W_self) and
+ * SMs left to NCCL while later chunks fly */
 BGNN_API int bgnn_dist_set_pipeline(bgnn_dist* d, uint32_t chunks, uint32_t reserve_sms);
 /* Fill the halo rows of x_ext ([n_own + n_halo, F], owned rows present)
  * with their owners' rows. */
 BGNN_API int bgnn_dist_exchange(bgnn_dist* d, const bgnn_part* p, float* x_ext,
                                 uint32_t num_features);
 /* Halo exchange + fused gather/scatter (MessagePassing.scatter{Add,Mean,Max},
- * sparse.ts:400-451) of the local rows: out [n_own, F].  The exchange runs
- * in column chunks and each chunk's columns are aggregated as soon as it has
- * landed; the halo rows of x_ext are filled as a side effect. */
+ * sparse.ts:400-451) of the local rows: out [n_own, F].  With several column
+ * chunks (bgnn_dist_set_pipeline) each chunk's columns are aggregated as soon
+ * as it has landed; the halo rows of x_ext are filled as a side effect. */
 BGNN_API int bgnn_dist_aggregate(bgnn_dist* d, const bgnn_part* p, int aggr, float* x_ext,
                                  uint32_t num_features, float* out);
 /* The same with per-entry values: the row-partitioned SparseCSR.matmul
