@@ -209,13 +209,14 @@ def sage_forward(layers, dg, x, timers=None):
     return h
 
 
-def dist_forward(layers, pgd, timers=None):
+def dist_forward(layers, pgd, timers=None, early=True):
     """The same three layers on one rank of the row partition
     (browsergnn_b200.distributed): each SAGEConv.forward on the
-    PartitionedGraphData exchanges its input's halo rows with NCCL in column
-    chunks pipelined with the aggregation, runs x * W_self on a side stream,
-    and writes its output into the owned rows of the next layer's
-    [owned | halo] buffer.  `timers` collects CUDA events around each layer."""
+    PartitionedGraphData runs x * W_self on a side stream while its input's
+    halo rows arrive over NCCL, aggregates, and writes its output into the
+    owned rows of the next layer's [owned | halo] buffer; with `early` the
+    next layer's halo rows are sent block by block while that last product
+    runs.  `timers` collects CUDA events around each layer."""
     import torch
 
     h = pgd
@@ -224,7 +225,8 @@ def dist_forward(layers, pgd, timers=None):
         if timers is not None:
             a = torch.cuda.Event(enable_timing=True)
             a.record()
-        h = lay.forward(h, _act="relu" if li < len(layers) - 1 else None)
+        last = li == len(layers) - 1
+        h = lay.forward(h, _act=None if last else "relu", _send_next=early and not last)
         if timers is not None:
             b = torch.cuda.Event(enable_timing=True)
             b.record()
@@ -434,8 +436,8 @@ def spmm_sweep(steps, warmup, hbm_peak, parity=True, dctx=None, rank=0, world=1)
     """The standalone CSR SpMM (SparseCSR.matmul) of the scale-24 R-MAT
     matrix with 2^28 entries at F = 32/64/128/256.  N>1: rows partitioned
     across the ranks (browsergnn_b200.distributed.PartitionedGraph.from_csr),
-    the halo rows of X exchanged with NCCL in column chunks pipelined with
-    the local SpMM; time = max over ranks."""
+    the halo rows of X exchanged with NCCL (grouped send/recv) before the
+    local SpMM; time = max over ranks."""
     import torch
 
     import browsergnn_b200 as bg
@@ -480,6 +482,11 @@ def spmm_sweep(steps, warmup, hbm_peak, parity=True, dctx=None, rank=0, world=1)
         pg = distributed.PartitionedGraph.from_csr(csr, world, rank)
         torch.cuda.synchronize()
         res["partition_plan_s"] = round(max_over_ranks(time.perf_counter() - t0), 3)
+        lrp = torch.empty(pg.n_own + 1, dtype=torch.int32, device="cuda")
+        ctx.call("bgnn_graph_csr", pg.graph, ptr(lrp), None, None)
+        deg = (lrp[1:] - lrp[:-1]).max().item() if pg.n_own else 0
+        res["max_row_entries_over_ranks"] = int(max_over_ranks(float(deg)))
+        del lrp
         res["parallelism"] = f"row-partition x{world}"
         res["scaling"] = "strong"
     per_f = {}
@@ -528,6 +535,32 @@ def spmm_sweep(steps, warmup, hbm_peak, parity=True, dctx=None, rank=0, world=1)
                                                   / (ms * 1e-3) / 1e9, 1)}
         if host_csr is not None and f in (32, 256):
             per_f[str(f)]["parity"] = spmm_parity(host_csr, x, out, f, seed)
+        if pg is not None:
+            # where the time goes: the exchange alone and the local SpMM alone
+            local_vals = csr.values[pg.entry_lo:pg.entry_lo + pg.num_local_edges]
+
+            def parts(fn):
+                for _ in range(2):
+                    fn()
+                torch.cuda.synchronize()
+                import torch.distributed as dist
+
+                dist.barrier()
+                a0 = torch.cuda.Event(enable_timing=True)
+                a1 = torch.cuda.Event(enable_timing=True)
+                a0.record()
+                for _ in range(steps):
+                    fn()
+                a1.record()
+                dctx.synchronize()
+                return round(max_over_ranks(a0.elapsed_time(a1) / steps), 3)
+
+            per_f[str(f)]["exchange_ms"] = parts(
+                lambda: ctx.call_on("bgnn_dist_exchange", dctx.h, pg.h, ptr(ext), f))
+            per_f[str(f)]["local_spmm_ms"] = parts(
+                lambda: ctx.call("bgnn_graph_spmm", pg.graph, ptr(local_vals), ptr(ext), f,
+                                 ptr(out)))
+            per_f[str(f)]["max_halo_rows"] = int(max_over_ranks(float(pg.n_halo)))
         if pg is not None and parity and f in (32, 256):
             # each rank's rows against a single-GPU SpMM of the whole matrix
             full = torch.empty((n, f), device="cuda")
@@ -1064,7 +1097,11 @@ def main():
                          "tensor: X*W on the tcgen05 tensor cores (3xTF32), with the count of "
                          "elements outside the parity bar reported")
     ap.add_argument("--chunks", type=int, default=None,
-                    help="N>1: column chunks of the pipelined halo exchange (0: by width)")
+                    help="N>1: column chunks of the halo exchange, each aggregated as it lands "
+                         "(default 1)")
+    ap.add_argument("--row-blocks", type=int, default=4,
+                    help="N>1: row blocks of each layer's last product whose rows are sent to "
+                         "the peers as they are written (0: no early sends)")
     ap.add_argument("--reserve-sms", type=int, default=16,
                     help="N>1: SMs the aggregation leaves to NCCL while chunks are in flight")
     ap.add_argument("--profile", choices=["small", "full-agg", "csr", "csr-small", "linear", "gat",
@@ -1088,6 +1125,7 @@ def main():
 
     import browsergnn_b200 as bg
     from browsergnn_b200 import synth
+    from browsergnn_b200.backend import ptr
 
     torch.cuda.set_device(local)
     if world > 1:
@@ -1124,6 +1162,8 @@ def main():
         dctx = distributed.DistContext(rank, world, device=local, timeout_ms=120_000)
         if args.chunks is not None:
             dctx.set_pipeline(args.chunks, args.reserve_sms)
+        if args.row_blocks:
+            dctx.set_row_blocks(args.row_blocks)
         torch.cuda.synchronize()
         nccl_init_s = max_over_ranks(time.perf_counter() - t0)
         t0 = time.perf_counter()
@@ -1133,7 +1173,8 @@ def main():
         pgd = distributed.PartitionedGraphData(pg, dctx, ext0, WIDTHS[0])
         x = ext0[: pg.n_own]
         dg = None
-        step = lambda timers=None: dist_forward(layers, pgd, timers)  # noqa: E731
+        early = args.row_blocks > 0
+        step = lambda timers=None: dist_forward(layers, pgd, timers, early)  # noqa: E731
     else:
         from browsergnn_b200.graph import DeviceGraph
 
@@ -1258,13 +1299,18 @@ def main():
     part_info = None
     if world > 1:
         pg = pgd.pg
+        lrp = torch.empty(pg.n_own + 1, dtype=torch.int32, device="cuda")
+        pg.ctx.call("bgnn_graph_csr", pg.graph, ptr(lrp), None, None)
         part_info = {"rows": pg.n_own, "halo_rows": pg.n_halo, "send_rows": pg.n_send,
-                     "local_edges": pg.num_local_edges}
+                     "local_edges": pg.num_local_edges,
+                     "max_row_edges": int((lrp[1:] - lrp[:-1]).max().item()) if pg.n_own else 0}
+        del lrp
         allinfo = [None] * world
         dist.all_gather_object(allinfo, part_info)
         part_info = {"per_rank": allinfo,
-                     "halo_exchange": "NCCL grouped send/recv in column chunks, pipelined "
-                                      "with the aggregation (browsergnn_b200.distributed)"}
+                     "halo_exchange": "NCCL grouped send/recv of the halo rows (one chunk of "
+                                      "columns by default), X*W_self on a side stream "
+                                      "meanwhile (browsergnn_b200.distributed)"}
         pgd = None
         pg.close()
     spmm = None
@@ -1286,6 +1332,7 @@ def main():
             "config": {"workload": "sage-mean-3layer-rmat-2450000n-62000000e",
                        "widths": WIDTHS, "edges_per_layer": e, "layers": 3,
                        "parallelism": f"row-partition x{world}" if world > 1 else "single",
+                       "early_send_row_blocks": (args.row_blocks if world > 1 else None),
                        "l2": "inputs larger than L2 (no flush)",
                        "math": ("fast (f32 fma in the reference's order)" if args.math == "fast"
                                 else "tensor (X*W on tcgen05, 3xTF32)"),

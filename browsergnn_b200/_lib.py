@@ -120,6 +120,7 @@ SIGNATURES = {
                        ctypes.POINTER(_U64), ctypes.POINTER(_U64), ctypes.POINTER(_U64)],
     "bgnn_part_bounds": [_P, ctypes.POINTER(_U32)],
     "bgnn_part_counts": [_P, ctypes.POINTER(_U64), ctypes.POINTER(_U64)],
+    "bgnn_part_row_blocks": [_P, _P, _U32, ctypes.POINTER(_U64), ctypes.POINTER(_U64)],
     "bgnn_part_graph": [_P, ctypes.POINTER(_P)],
     "bgnn_part_lists": [_P, _P, _P, _P],
     "bgnn_part_pack": [_P, _P, _P, _U64, _U32, _U32, _P],
@@ -133,6 +134,8 @@ SIGNATURES = {
     "bgnn_dist_aggregate": [_P, _P, _I, _P, _U32, _P],
     "bgnn_dist_spmm": [_P, _P, _P, _P, _U32, _P],
     "bgnn_dist_sage_layer": [_P, _P, _I, _P, _U32, _U32, _P, _P, _P, _I, _D, _P, _P],
+    "bgnn_dist_sage_layer_ex": [_P, _P, _I, _P, _U32, _U32, _P, _P, _P, _I, _D, _P, _P, _U32],
+    "bgnn_dist_set_row_blocks": [_P, _U32],
     "bgnn_dist_allreduce_max": [_P, ctypes.POINTER(_D), _U32],
     "bgnn_dist_synchronize": [_P],
 }

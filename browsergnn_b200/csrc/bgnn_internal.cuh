@@ -72,7 +72,25 @@ struct bgnn_part {
   uint64_t n_send = 0;
   std::vector<uint64_t> send_counts, recv_counts;  // rows per peer
   std::vector<uint64_t> send_off, recv_off;        // exclusive prefix of the counts
+  // Row blocks, for halo sends that start as each block of a layer's output
+  // is written: every rank's owned rows cut into blk_count blocks (block c of
+  // n rows: [c n / C, (c+1) n / C)); blk_send[q (C+1) + c] is the first entry
+  // of peer q's send list in block c, blk_recv[q (C+1) + c] the first halo
+  // slot of owner q's block c (host copies; blk_send also on the device).
+  // Derived on first use and kept.
+  mutable uint32_t blk_count = 0;
+  mutable std::vector<uint64_t> blk_send, blk_recv;
+  mutable uint64_t* d_blk_send = nullptr;
 };
+// the first owned row of block c of `blocks` over n rows
+inline uint32_t bgnn_block_row(uint32_t n, uint32_t blocks, uint32_t c) {
+  return (uint32_t)((uint64_t)c * n / blocks);
+}
+int bgnn_part_row_blocks(bgnn_ctx* ctx, const bgnn_part* p, uint32_t blocks);
+// pack block c's send rows (every peer's) of x ([n_own, width] rows at
+// stride width) into out at their send-list positions
+int bgnn_run_pack_block(bgnn_ctx* ctx, const float* x, uint32_t width, const bgnn_part* p,
+                        uint32_t c, float* out);
 void bgnn_part_free(bgnn_part* p);
 int bgnn_run_pack_cols(bgnn_ctx* ctx, const float* x, uint64_t ld_x, uint32_t col0,
                        uint32_t width, const uint32_t* rows, uint64_t n, float* out);

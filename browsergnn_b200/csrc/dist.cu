@@ -14,6 +14,12 @@
 // in edge order) starts as soon as chunk c has landed, leaving `reserve` SMs
 // to the NCCL kernels while later chunks are in flight.
 //
+// Early sends (BGNN_DIST_SEND_OUT): when a layer's output is the next
+// layer's [owned | halo] buffer, the layer's last product runs in row blocks
+// and each block's rows are packed and sent as soon as the block is written,
+// so the next layer's exchange overlaps this layer's product; the next layer
+// then finds its halo in flight and only waits for it.
+//
 // Timeouts: the communicator is created non-blocking and every piece of NCCL
 // work is watched by a thread that aborts the communicator when the work is
 // not done by its deadline (timeout_ms after it was enqueued) or NCCL reports
@@ -119,6 +125,14 @@ struct bgnn_dist {
   uint64_t st_cap = 0;
   uint32_t chunks = 0;                  // 0: chosen per call from the width
   uint32_t reserve_sms = 16;            // SMs the aggregation leaves to NCCL while chunks fly
+  // early sends: row blocks of the last product, their events, and the
+  // buffer whose exchange is in flight (landed at ev_early)
+  uint32_t row_blocks = 4;
+  cudaEvent_t ev_rows[kMaxChunks] = {};
+  cudaEvent_t ev_early = nullptr;
+  const float* early_buf = nullptr;
+  const bgnn_part* early_part = nullptr;
+  uint32_t early_f = 0;
   // watchdog
   std::mutex mu;
   std::condition_variable cv;
@@ -308,13 +322,84 @@ int enqueue_chunk(bgnn_dist* d, const bgnn_part* p, float* x_ext, uint32_t f, ui
   return watch_locked(d, done);
 }
 
+// x_ext's halo exchange already in flight (started by the layer that wrote
+// it, BGNN_DIST_SEND_OUT): the caller's stream waits for it, and true
+bool take_early(bgnn_dist* d, const bgnn_part* p, const float* x_ext, uint32_t f) {
+  if (!x_ext || d->early_buf != x_ext || d->early_part != p || d->early_f != f) return false;
+  d->early_buf = nullptr;
+  d->early_part = nullptr;
+  d->early_f = 0;
+  return cudaStreamWaitEvent(d->ctx->stream, d->ev_early, 0) == cudaSuccess;
+}
+
+// The layer's last product, out[r] = act(f32(f32(st[r] + agg[r] * w) + bias))
+// (st NULL: act(f32(agg[r] * w + bias))), in row blocks; each block's send
+// rows are packed and sent to the peers as soon as the block is written,
+// and the peers' blocks land in out's halo rows.  out: the next layer's
+// [n_own + n_halo, n] buffer.
+int product_and_send(bgnn_dist* d, const bgnn_part* p, const float* agg, const float* w,
+                     uint32_t k, uint32_t n, const float* st, const float* bias, int act,
+                     double act_param, float* out) {
+  bgnn_ctx* ctx = d->ctx;
+  const uint32_t C = d->row_blocks;
+  BGNN_TRY(bgnn_part_row_blocks(ctx, p, C));
+  BGNN_TRY(ensure(d, &d->send_buf, &d->send_cap, p->n_send * (uint64_t)n + 4));
+  const NcclApi& api = nccl();
+  const uint32_t m = p->n_own;
+  for (uint32_t c = 0; c < C; c++) {
+    const uint32_t r0 = bgnn_block_row(m, C, c), r1 = bgnn_block_row(m, C, c + 1);
+    if (r1 > r0) {
+      const uint64_t o = r0;
+      if (st)
+        BGNN_TRY(bgnn_run_linear_add(ctx, agg + o * k, w, r1 - r0, k, n, st + o * n, bias, act,
+                                     act_param, out + o * n));
+      else
+        BGNN_TRY(bgnn_run_linear(ctx, agg + o * k, w, nullptr, nullptr, r1 - r0, k, n, bias, act,
+                                 act_param, out + o * n));
+    }
+    BGNN_CUDA(ctx, cudaEventRecord(d->ev_rows[c], ctx->stream));
+    BGNN_CUDA(ctx, cudaStreamWaitEvent(d->nccl_stream, d->ev_rows[c], 0));
+    {
+      StreamSwap sw(ctx, d->nccl_stream);
+      BGNN_TRY(bgnn_run_pack_block(ctx, out, n, p, c, d->send_buf));
+    }
+    std::lock_guard<std::mutex> lk(d->mu);
+    BGNN_TRY(dist_fail(d));
+    const auto deadline = Clock::now() + std::chrono::milliseconds(d->timeout_ms);
+    ncclResult_t r = api.GroupStart();
+    for (uint32_t q = 0; q < d->world && (r == ncclSuccess || r == ncclInProgress); q++) {
+      if (q == d->rank) continue;
+      const uint64_t* bs = p->blk_send.data() + (uint64_t)q * (C + 1);
+      const uint64_t* br = p->blk_recv.data() + (uint64_t)q * (C + 1);
+      if (bs[c + 1] > bs[c])
+        r = api.Send(d->send_buf + bs[c] * n, (bs[c + 1] - bs[c]) * n, ncclFloat32, (int)q, d->comm,
+                     d->nccl_stream);
+      if ((r == ncclSuccess || r == ncclInProgress) && br[c + 1] > br[c])
+        r = api.Recv(out + (m + br[c]) * (uint64_t)n, (br[c + 1] - br[c]) * n, ncclFloat32, (int)q,
+                     d->comm, d->nccl_stream);
+    }
+    const ncclResult_t r2 = api.GroupEnd();
+    if (r == ncclSuccess || r == ncclInProgress) r = r2;
+    if (r != ncclSuccess && r != ncclInProgress) {
+      abort_locked(d, BGNN_ERR_CUDA, std::string("NCCL send/recv: ") + api.GetErrorString(r));
+      return dist_fail(d);
+    }
+    BGNN_TRY(wait_enqueued_locked(d, deadline));
+    if (c + 1 == C) BGNN_TRY(watch_locked(d, d->ev_early));
+  }
+  d->early_buf = out;
+  d->early_part = p;
+  d->early_f = n;
+  return BGNN_OK;
+}
+
 // exchange + per-chunk aggregation of x_ext ([n_own + n_halo, f], owned rows
 // present) into out ([n_own, f]); aggr as bgnn_aggregate_strided
 int exchange_aggregate(bgnn_dist* d, const bgnn_part* p, int aggr, const float* values,
                        float* x_ext, uint32_t f, float* out) {
   bgnn_ctx* ctx = d->ctx;
   const bgnn_graph* g = &p->local;
-  if (d->world == 1 || f == 0)
+  if (d->world == 1 || f == 0 || take_early(d, p, x_ext, f))
     return bgnn_run_aggregate_cols(ctx, g, aggr, values, x_ext, f, f, out, f);
   const uint32_t chunks = pick_chunks(d, f);
   BGNN_TRY(ensure(d, &d->send_buf, &d->send_cap, p->n_send * (uint64_t)f + 4));
@@ -397,8 +482,11 @@ extern "C" int bgnn_dist_create(bgnn_ctx* ctx, const uint8_t* unique_id, uint32_
   ok = ok && cudaStreamCreateWithFlags(&d->side_stream, cudaStreamNonBlocking) == cudaSuccess;
   ok = ok && cudaEventCreateWithFlags(&d->ev_start, cudaEventDisableTiming) == cudaSuccess;
   ok = ok && cudaEventCreateWithFlags(&d->ev_side, cudaEventDisableTiming) == cudaSuccess;
-  for (int c = 0; c < kMaxChunks; c++)
+  for (int c = 0; c < kMaxChunks; c++) {
     ok = ok && cudaEventCreateWithFlags(&d->ev_chunk[c], cudaEventDisableTiming) == cudaSuccess;
+    ok = ok && cudaEventCreateWithFlags(&d->ev_rows[c], cudaEventDisableTiming) == cudaSuccess;
+  }
+  ok = ok && cudaEventCreateWithFlags(&d->ev_early, cudaEventDisableTiming) == cudaSuccess;
   if (!ok) {
     cudaGetLastError();
     bgnn_dist_destroy(d);
@@ -459,8 +547,11 @@ extern "C" int bgnn_dist_destroy(bgnn_dist* d) {
   for (auto ev : d->spare) cudaEventDestroy(ev);
   if (d->ev_start) cudaEventDestroy(d->ev_start);
   if (d->ev_side) cudaEventDestroy(d->ev_side);
-  for (int c = 0; c < kMaxChunks; c++)
+  for (int c = 0; c < kMaxChunks; c++) {
     if (d->ev_chunk[c]) cudaEventDestroy(d->ev_chunk[c]);
+    if (d->ev_rows[c]) cudaEventDestroy(d->ev_rows[c]);
+  }
+  if (d->ev_early) cudaEventDestroy(d->ev_early);
   cudaFree(d->send_buf);
   cudaFree(d->recv_buf);
   cudaFree(d->st_buf);
@@ -491,7 +582,8 @@ extern "C" int bgnn_dist_exchange(bgnn_dist* d, const bgnn_part* p, float* x_ext
   BGNN_TRY(dist_ok(d));
   BGNN_TRY(part_matches(d, p));
   BGNN_REQUIRE(d->ctx, x_ext || (uint64_t)(p->n_own + p->n_halo) * num_features == 0, "NULL x_ext");
-  if (d->world == 1 || num_features == 0) return BGNN_OK;
+  if (d->world == 1 || num_features == 0 || take_early(d, p, x_ext, num_features))
+    return BGNN_OK;
   bgnn_ctx* ctx = d->ctx;
   BGNN_TRY(ensure(d, &d->send_buf, &d->send_cap, p->n_send * (uint64_t)num_features + 4));
   BGNN_CUDA(ctx, cudaEventRecord(d->ev_start, ctx->stream));
@@ -526,16 +618,37 @@ extern "C" int bgnn_dist_sage_layer(bgnn_dist* d, const bgnn_part* p, int aggr, 
                                     uint32_t k, uint32_t n, const float* w_neigh,
                                     const float* w_self, const float* bias, int act,
                                     double act_param, float* agg, float* out) {
+  return bgnn_dist_sage_layer_ex(d, p, aggr, x_ext, k, n, w_neigh, w_self, bias, act, act_param,
+                                 agg, out, 0u);
+}
+
+extern "C" int bgnn_dist_set_row_blocks(bgnn_dist* d, uint32_t blocks) {
+  BGNN_TRY(dist_ok(d));
+  BGNN_REQUIRE(d->ctx, blocks >= 1 && blocks <= (uint32_t)kMaxChunks, "row blocks %u outside [1, %d]",
+               blocks, kMaxChunks);
+  d->row_blocks = blocks;
+  return BGNN_OK;
+}
+
+extern "C" int bgnn_dist_sage_layer_ex(bgnn_dist* d, const bgnn_part* p, int aggr, float* x_ext,
+                                       uint32_t k, uint32_t n, const float* w_neigh,
+                                       const float* w_self, const float* bias, int act,
+                                       double act_param, float* agg, float* out, uint32_t flags) {
   BGNN_TRY(dist_ok(d));
   BGNN_TRY(part_matches(d, p));
   bgnn_ctx* ctx = d->ctx;
   BGNN_REQUIRE(ctx, aggr >= BGNN_AGGR_SUM && aggr <= BGNN_AGGR_MAX, "unknown aggregation %d", aggr);
   BGNN_REQUIRE(ctx, act >= BGNN_ACT_NONE && act <= BGNN_ACT_SILU, "unknown activation %d", act);
+  BGNN_REQUIRE(ctx, (flags & ~BGNN_DIST_SEND_OUT) == 0, "unknown flags 0x%x", flags);
   const uint64_t m = p->n_own;
   BGNN_REQUIRE(ctx, (x_ext && agg && out && w_neigh) || m * k * n == 0, "NULL argument");
+  const bool send_out = (flags & BGNN_DIST_SEND_OUT) && d->world > 1;
   if (m == 0 || n == 0) {
-    // a rank without rows still takes part in the exchange its peers wait for
-    return k ? exchange_aggregate(d, p, aggr, nullptr, x_ext, k, agg) : BGNN_OK;
+    // a rank without rows still takes part in the exchanges its peers wait for
+    if (k) BGNN_TRY(exchange_aggregate(d, p, aggr, nullptr, x_ext, k, agg));
+    return send_out && n ? product_and_send(d, p, agg, w_neigh, k, n, nullptr, bias, act,
+                                            act_param, out)
+                         : BGNN_OK;
   }
   const bool root = w_self != nullptr;
   if (root) {
@@ -551,8 +664,11 @@ extern "C" int bgnn_dist_sage_layer(bgnn_dist* d, const bgnn_part* p, int aggr, 
     BGNN_CUDA(ctx, cudaEventRecord(d->ev_side, d->side_stream));
   }
   BGNN_TRY(exchange_aggregate(d, p, aggr, nullptr, x_ext, k, agg));
+  if (root) BGNN_CUDA(ctx, cudaStreamWaitEvent(ctx->stream, d->ev_side, 0));
+  if (send_out)
+    return product_and_send(d, p, agg, w_neigh, k, n, root ? d->st_buf : nullptr, bias, act,
+                            act_param, out);
   if (root) {
-    BGNN_CUDA(ctx, cudaStreamWaitEvent(ctx->stream, d->ev_side, 0));
     // out = act(f32(f32(St + agg * W_neigh) + bias)): the two f32 products and
     // the final rounding of bgnn_sage_linear
     return bgnn_run_linear_add(ctx, agg, w_neigh, (uint32_t)m, k, n, d->st_buf, bias, act,

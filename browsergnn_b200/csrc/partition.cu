@@ -187,6 +187,66 @@ __global__ void k_unpack_cols(const float* __restrict__ src, uint64_t n, uint32_
   }
 }
 
+// first index i in [0, len) with a[i] >= key (len when none)
+__device__ __forceinline__ uint64_t lower_bound_u32(const uint32_t* a, uint64_t len, uint32_t key) {
+  uint64_t lo = 0, hi = len;
+  while (lo < hi) {
+    const uint64_t mid = (lo + hi) >> 1;
+    if (a[mid] < key)
+      lo = mid + 1;
+    else
+      hi = mid;
+  }
+  return lo;
+}
+
+// one thread per (peer q, block boundary c): where block c starts in peer q's
+// send list (owned local ids, ascending) and in owner q's halo slots (global
+// ids, ascending)
+__global__ void k_row_blocks(const uint32_t* __restrict__ send_rows,
+                             const uint32_t* __restrict__ halo_ids,
+                             const uint64_t* __restrict__ offs,  // send_off [w+1], recv_off [w+1]
+                             const uint32_t* __restrict__ bounds, uint32_t world, uint32_t rank,
+                             uint32_t blocks, uint64_t* __restrict__ out_send,
+                             uint64_t* __restrict__ out_recv) {
+  const uint32_t t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= world * (blocks + 1)) return;
+  const uint32_t q = t / (blocks + 1), c = t % (blocks + 1);
+  const uint64_t* send_off = offs;
+  const uint64_t* recv_off = offs + world + 1;
+  const uint32_t n_own = bounds[rank + 1] - bounds[rank];
+  const uint32_t key = (uint32_t)((uint64_t)c * n_own / blocks);
+  out_send[t] = send_off[q] + lower_bound_u32(send_rows + send_off[q],
+                                              send_off[q + 1] - send_off[q], key);
+  const uint32_t nq = bounds[q + 1] - bounds[q];
+  const uint32_t gkey = bounds[q] + (uint32_t)((uint64_t)c * nq / blocks);
+  out_recv[t] = recv_off[q] + lower_bound_u32(halo_ids + recv_off[q],
+                                              recv_off[q + 1] - recv_off[q], gkey);
+}
+
+// out[i, :] = x[rows[i], :] for the entries of block c of every peer
+// (blockIdx.y = peer)
+template <int V>
+__global__ void k_pack_block(const float* __restrict__ x, uint32_t width,
+                             const uint32_t* __restrict__ rows, const uint64_t* __restrict__ blk,
+                             uint32_t blocks, uint32_t c, float* __restrict__ out) {
+  const uint32_t q = blockIdx.y;
+  const uint64_t b = blk[q * (blocks + 1) + c], e = blk[q * (blocks + 1) + c + 1];
+  const uint32_t wv = width / V;
+  const uint64_t total = (e - b) * wv;
+  for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+       t += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t i = b + t / wv;
+    const uint32_t j = (uint32_t)(t % wv) * V;
+    const float* src = x + (uint64_t)rows[i] * width + j;
+    float* dst = out + i * width + j;
+    if constexpr (V == 4)
+      *reinterpret_cast<float4*>(dst) = __ldg(reinterpret_cast<const float4*>(src));
+    else
+      *dst = __ldg(src);
+  }
+}
+
 // The plan from a square device CSR (row_ptr [n+1], col [nnz]).
 int build_part(bgnn_ctx* ctx, const uint32_t* rp, const uint32_t* col, uint32_t n,
                uint32_t world, uint32_t rank, bgnn_part* p) {
@@ -333,8 +393,68 @@ void bgnn_part_free(bgnn_part* p) {
   bgnn_graph_free(&p->local);
   cudaFree(p->halo_ids);
   cudaFree(p->send_rows);
+  cudaFree(p->d_blk_send);
   p->halo_ids = nullptr;
   p->send_rows = nullptr;
+  p->d_blk_send = nullptr;
+  p->blk_count = 0;
+}
+
+int bgnn_part_row_blocks(bgnn_ctx* ctx, const bgnn_part* p, uint32_t blocks) {
+  if (blocks == 0) return bgnn_set_error(ctx, BGNN_ERR_INVALID_ARG, "zero row blocks");
+  if (p->blk_count == blocks) return BGNN_OK;
+  const uint32_t w = p->world;
+  const uint64_t cells = (uint64_t)w * (blocks + 1);
+  cudaFree(p->d_blk_send);
+  p->d_blk_send = nullptr;
+  p->blk_count = 0;
+  BGNN_CUDA(ctx, cudaMalloc(&p->d_blk_send, cells * 8));
+  DevTmp recv, offs, bnd;
+  BGNN_TRY(bgnn_tmp_alloc(ctx, recv, cells * 8));
+  BGNN_TRY(bgnn_tmp_alloc(ctx, offs, (uint64_t)(w + 1) * 16));
+  BGNN_TRY(bgnn_tmp_alloc(ctx, bnd, (uint64_t)(w + 1) * 4));
+  std::vector<uint64_t> h_offs(2 * (w + 1));
+  std::copy(p->send_off.begin(), p->send_off.end(), h_offs.begin());
+  std::copy(p->recv_off.begin(), p->recv_off.end(), h_offs.begin() + w + 1);
+  BGNN_CUDA(ctx, cudaMemcpyAsync(offs.p, h_offs.data(), h_offs.size() * 8, cudaMemcpyHostToDevice,
+                                 ctx->stream));
+  BGNN_CUDA(ctx, cudaMemcpyAsync(bnd.p, p->bounds.data(), (w + 1) * 4, cudaMemcpyHostToDevice,
+                                 ctx->stream));
+  k_row_blocks<<<(unsigned)((cells + 127) / 128), 128, 0, ctx->stream>>>(
+      p->send_rows, p->halo_ids, offs.as<uint64_t>(), bnd.as<uint32_t>(), w, p->rank, blocks,
+      p->d_blk_send, recv.as<uint64_t>());
+  BGNN_LAUNCHED(ctx);
+  p->blk_send.assign(cells, 0);
+  p->blk_recv.assign(cells, 0);
+  BGNN_CUDA(ctx, cudaMemcpyAsync(p->blk_send.data(), p->d_blk_send, cells * 8,
+                                 cudaMemcpyDeviceToHost, ctx->stream));
+  BGNN_CUDA(ctx, cudaMemcpyAsync(p->blk_recv.data(), recv.p, cells * 8, cudaMemcpyDeviceToHost,
+                                 ctx->stream));
+  BGNN_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  p->blk_count = blocks;
+  return BGNN_OK;
+}
+
+int bgnn_run_pack_block(bgnn_ctx* ctx, const float* x, uint32_t width, const bgnn_part* p,
+                        uint32_t c, float* out) {
+  const uint32_t C = p->blk_count;
+  if (C == 0 || c >= C) return bgnn_set_error(ctx, BGNN_ERR_INVALID_ARG, "row block %u of %u", c, C);
+  if (width == 0 || p->n_send == 0 || p->world < 2) return BGNN_OK;
+  const bool v4 = width % 4 == 0 && (uintptr_t)x % 16 == 0 && (uintptr_t)out % 16 == 0;
+  const uint64_t per_peer = p->n_send / C / (p->world - 1) + 1;
+  const uint64_t work = per_peer * (v4 ? width / 4 : width);
+  uint64_t gx = (work + 255) / 256;
+  const uint64_t cap = (uint64_t)ctx->num_sms * 8 / p->world + 1;
+  if (gx > cap) gx = cap;
+  dim3 grid((unsigned)gx, p->world);
+  if (v4)
+    k_pack_block<4><<<grid, 256, 0, ctx->stream>>>(x, width, p->send_rows, p->d_blk_send, C, c,
+                                                   out);
+  else
+    k_pack_block<1><<<grid, 256, 0, ctx->stream>>>(x, width, p->send_rows, p->d_blk_send, C, c,
+                                                   out);
+  BGNN_LAUNCHED(ctx);
+  return BGNN_OK;
 }
 
 int bgnn_run_pack_cols(bgnn_ctx* ctx, const float* x, uint64_t ld_x, uint32_t col0,
@@ -456,6 +576,17 @@ extern "C" int bgnn_part_counts(const bgnn_part* p, uint64_t* send_rows, uint64_
   if (!p) return BGNN_ERR_INVALID_ARG;
   if (send_rows) std::copy(p->send_counts.begin(), p->send_counts.end(), send_rows);
   if (recv_rows) std::copy(p->recv_counts.begin(), p->recv_counts.end(), recv_rows);
+  return BGNN_OK;
+}
+
+extern "C" int bgnn_part_row_blocks(bgnn_ctx* ctx, const bgnn_part* p, uint32_t blocks,
+                                    uint64_t* send_first, uint64_t* recv_first) {
+  if (!ctx || !p) return BGNN_ERR_INVALID_ARG;
+  BGNN_CUDA(ctx, cudaSetDevice(p->device));
+  BGNN_REQUIRE(ctx, blocks >= 1 && blocks <= 64, "row blocks %u outside [1, 64]", blocks);
+  BGNN_TRY(bgnn_part_row_blocks(ctx, p, blocks));
+  if (send_first) std::copy(p->blk_send.begin(), p->blk_send.end(), send_first);
+  if (recv_first) std::copy(p->blk_recv.begin(), p->blk_recv.end(), recv_first);
   return BGNN_OK;
 }
 

@@ -81,9 +81,15 @@ class DistContext:
         dist.broadcast_object_list(obj, src=0)
         return obj[0]
 
+    def set_row_blocks(self, blocks: int = 4):
+        """Row blocks of a layer's last product whose rows are sent to the
+        peers as each is written (sage_forward(send_next=True))."""
+        self.ctx.call_on("bgnn_dist_set_row_blocks", self.h, int(blocks))
+
     def set_pipeline(self, chunks: int = 0, reserve_sms: int = 16):
-        """Column chunks of the pipelined halo exchange (0: by width) and the
-        SMs the aggregation leaves to NCCL while later chunks are in flight."""
+        """Column chunks of the halo exchange, each aggregated as it lands
+        (0: the default, one chunk), and the SMs the aggregation leaves to
+        NCCL while later chunks are in flight."""
         self.ctx.call_on("bgnn_dist_set_pipeline", self.h, int(chunks), int(reserve_sms))
 
     def allreduce_max(self, values: Sequence[float]) -> List[float]:
@@ -189,6 +195,17 @@ class PartitionedGraph:
         return (hid[: self.n_halo].to(torch.int64) & 0xFFFFFFFF,
                 srow[: self.n_send].to(torch.int64) & 0xFFFFFFFF)
 
+    def row_blocks(self, blocks: int):
+        """(send_first, recv_first) as [world, blocks + 1] uint64 arrays: where
+        each row block starts in each peer's send list and in each owner's
+        halo slots (bgnn_part_row_blocks)."""
+        w = self.world
+        s = (ctypes.c_uint64 * (w * (blocks + 1)))()
+        r = (ctypes.c_uint64 * (w * (blocks + 1)))()
+        self.ctx.call("bgnn_part_row_blocks", self.h, int(blocks), s, r)
+        return (np.ctypeslib.as_array(s).reshape(w, blocks + 1).copy(),
+                np.ctypeslib.as_array(r).reshape(w, blocks + 1).copy())
+
     def aggregate(self, dist: DistContext, x_ext, aggr: str = "mean", out=None):
         """Halo exchange + sum / mean / max aggregation of the owned rows."""
         torch = _torch()
@@ -257,11 +274,21 @@ def partition(graph, dist: DistContext) -> PartitionedGraphData:
     return PartitionedGraphData(pg, dist, ext, graph.numFeatures)
 
 
-def sage_forward(layer, input: PartitionedGraphData, act=None) -> PartitionedGraphData:
+SEND_OUT = 1  # BGNN_DIST_SEND_OUT
+
+
+def sage_forward(layer, input: PartitionedGraphData, act=None,
+                 send_next: bool = False) -> PartitionedGraphData:
     """SAGEConv.forward (sage.ts:113-217) on one rank of a partitioned graph:
-    halo exchange in column chunks pipelined with the aggregation, the root
-    product on a side stream, the fused linear writing the owned rows of the
-    next layer's [owned | halo] buffer."""
+    halo exchange (column chunks pipelined with the aggregation when the
+    context asks for them), the root product on a side stream, the fused
+    linear writing the owned rows of the next layer's [owned | halo] buffer.
+
+    send_next: another layer reads this one's output, so its halo exchange
+    starts while this layer's last product runs (row blocks sent as they are
+    written).  Every rank passes the same value.  Layers whose output changes
+    after the product (normalize) or that aggregate a projection (pool) send
+    nothing early."""
     from .layers import _act_code
 
     torch = _torch()
@@ -289,9 +316,10 @@ def sage_forward(layer, input: PartitionedGraphData, act=None) -> PartitionedGra
         pg.ctx.call("bgnn_sage_linear", ptr(agg), ptr(input.x_ext), ptr(layer.p("lin_neighbor")),
                     ptr(w_self), pg.n_own, k, n, ptr(layer.p("bias")), code, param, ptr(out_ext))
     else:
-        pg.ctx.call_on("bgnn_dist_sage_layer", dist.h, pg.h, _lib.AGGR[layer.aggregator],
+        flags = SEND_OUT if send_next and not layer.normalize else 0
+        pg.ctx.call_on("bgnn_dist_sage_layer_ex", dist.h, pg.h, _lib.AGGR[layer.aggregator],
                        ptr(input.x_ext), k, n, ptr(layer.p("lin_neighbor")), ptr(w_self),
-                       ptr(layer.p("bias")), code, param, ptr(agg), ptr(out_ext))
+                       ptr(layer.p("bias")), code, param, ptr(agg), ptr(out_ext), flags)
     if layer.normalize:
         pg.ctx.call("bgnn_l2_normalize_rows", ptr(out_ext), pg.n_own, n)
         if act is not None:

@@ -362,12 +362,14 @@ class SAGEConv(Module):
         ctx.call("bgnn_aggregate", dg.h, _lib.AGGR[aggr], ptr(src), self.inChannels, ptr(agg))
         return agg
 
-    def forward(self, input: GraphData, _act=None) -> GraphData:
+    def forward(self, input: GraphData, _act=None, _send_next: bool = False) -> GraphData:
         if getattr(input, "pg", None) is not None:
-            # one rank's share of a row-partitioned graph (distributed.partition)
+            # one rank's share of a row-partitioned graph (distributed.partition);
+            # _send_next: another layer reads the output (its halo exchange
+            # starts while this layer's last product runs)
             from .distributed import sage_forward
 
-            return sage_forward(self, input, _act)
+            return sage_forward(self, input, _act, send_next=_send_next)
         torch = _torch()
         dg, x = _prepare(self, input, self.inChannels, "SAGEConv")
         ctx = dg.ctx

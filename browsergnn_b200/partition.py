@@ -124,3 +124,56 @@ def exchange(plan: RowPlan, x_ext, group=None):
     dist.all_to_all_single(recv, send.contiguous(), plan.recv_counts, plan.send_counts,
                            group=group)
     return x_ext
+
+
+def block_row(n: int, blocks: int, c: int) -> int:
+    """First owned row of row block c of `blocks` over n rows."""
+    return (c * n) // blocks
+
+
+def row_blocks(plan: RowPlan, blocks: int):
+    """(send_first, recv_first), [world, blocks + 1] int64 each: where row
+    block c of this rank's rows starts in peer q's send list, and where owner
+    q's block c starts in the halo slots (entry / slot indices as in the
+    plan's lists).  The host restatement of bgnn_part_row_blocks."""
+    w = plan.world
+    send_off = np.concatenate([[0], np.cumsum(plan.send_counts)]).astype(np.int64)
+    recv_off = np.concatenate([[0], np.cumsum(plan.recv_counts)]).astype(np.int64)
+    cs = np.arange(blocks + 1, dtype=np.int64)
+    send_first = np.zeros((w, blocks + 1), np.int64)
+    recv_first = np.zeros((w, blocks + 1), np.int64)
+    for q in range(w):
+        seg = plan.send_rows[send_off[q]:send_off[q + 1]]
+        send_first[q] = send_off[q] + np.searchsorted(seg, (cs * plan.n_own) // blocks)
+        nq = plan.bounds[q + 1] - plan.bounds[q]
+        hseg = plan.halo_ids[recv_off[q]:recv_off[q + 1]]
+        recv_first[q] = recv_off[q] + np.searchsorted(hseg, plan.bounds[q] + (cs * nq) // blocks)
+    return send_first, recv_first
+
+
+def exchange_blocks(plan: RowPlan, x_ext, blocks: int, group=None):
+    """exchange() one row block at a time, the order of the early sends: for
+    each block c, every rank sends the rows of its block c that each peer
+    reads and receives each owner's block c into their halo slots."""
+    import torch
+    import torch.distributed as dist
+
+    sf, rf = row_blocks(plan, blocks)
+    n = plan.n_own
+    rows = torch.as_tensor(plan.send_rows, dtype=torch.long, device=x_ext.device)
+    for c in range(blocks):
+        ops = []
+        for q in range(plan.world):
+            if q == plan.rank:
+                continue
+            if sf[q, c + 1] > sf[q, c]:
+                ops.append(dist.P2POp(dist.isend, x_ext.index_select(
+                    0, rows[sf[q, c]:sf[q, c + 1]]).contiguous(), q, group=group))
+            if rf[q, c + 1] > rf[q, c]:
+                ops.append(dist.P2POp(dist.irecv, x_ext[n + rf[q, c]:n + rf[q, c + 1]], q,
+                                      group=group))
+        if ops:
+            for r in dist.batch_isend_irecv(ops):
+                r.wait()
+    return x_ext
+

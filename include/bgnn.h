@@ -385,6 +385,14 @@ BGNN_API int bgnn_part_info(const bgnn_part* p, uint32_t* row_lo, uint32_t* row_
 BGNN_API int bgnn_part_bounds(const bgnn_part* p, uint32_t* bounds);
 /* rows this rank sends to / receives from each rank (host arrays of world) */
 BGNN_API int bgnn_part_counts(const bgnn_part* p, uint64_t* send_rows, uint64_t* recv_rows);
+/* Row blocks (the early halo sends of bgnn_dist_sage_layer_ex): every
+ * rank's owned rows cut into `blocks` blocks, block c of n rows being rows
+ * [c*n/blocks, (c+1)*n/blocks).  Host arrays of world * (blocks + 1), either
+ * may be NULL: send_first[q*(blocks+1) + c] = the first entry of peer q's
+ * send list in this rank's block c (entry indices as in bgnn_part_lists),
+ * recv_first[q*(blocks+1) + c] = the first halo slot of owner q's block c. */
+BGNN_API int bgnn_part_row_blocks(bgnn_ctx* ctx, const bgnn_part* p, uint32_t blocks,
+                                  uint64_t* send_first, uint64_t* recv_first);
 /* the local graph (owned by the partition; valid until bgnn_part_destroy) */
 BGNN_API int bgnn_part_graph(const bgnn_part* p, const bgnn_graph** out);
 /* copies of the plan's lists (device buffers; either may be NULL): the
@@ -456,6 +464,21 @@ BGNN_API int bgnn_dist_sage_layer(bgnn_dist* d, const bgnn_part* p, int aggr, fl
                                   uint32_t k, uint32_t n, const float* w_neigh,
                                   const float* w_self, const float* bias, int act,
                                   double act_param, float* agg, float* out);
+/* bgnn_dist_sage_layer with flags.  BGNN_DIST_SEND_OUT: out is the owned
+ * rows of the next layer's [n_own + n_halo, n] buffer, and its halo exchange
+ * starts while the layer's last product is still running: the product runs
+ * in row blocks (bgnn_dist_set_row_blocks) and each block's rows go to the
+ * peers as soon as it is written.  The next bgnn_dist_sage_layer /
+ * _aggregate / _exchange on that buffer (same partition, width n) finds its
+ * halo in flight and only waits for it.  Every rank passes the same flags
+ * (the sends pair up across ranks). */
+#define BGNN_DIST_SEND_OUT 1u
+BGNN_API int bgnn_dist_sage_layer_ex(bgnn_dist* d, const bgnn_part* p, int aggr, float* x_ext,
+                                     uint32_t k, uint32_t n, const float* w_neigh,
+                                     const float* w_self, const float* bias, int act,
+                                     double act_param, float* agg, float* out, uint32_t flags);
+/* row blocks of BGNN_DIST_SEND_OUT (1..8; default 4) */
+BGNN_API int bgnn_dist_set_row_blocks(bgnn_dist* d, uint32_t blocks);
 /* Element-wise maximum over the ranks of count host doubles, in place
  * (timing); synchronises. */
 BGNN_API int bgnn_dist_allreduce_max(bgnn_dist* d, double* values, uint32_t count);

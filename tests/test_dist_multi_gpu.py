@@ -53,7 +53,7 @@ def _share_id(rank, world, ids):
     return ids.get()
 
 
-def _layers_main(rank, world, q, ids, go, chunks):
+def _layers_main(rank, world, q, ids, go, chunks, blocks):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     import torch
 
@@ -84,11 +84,15 @@ def _layers_main(rank, world, q, ids, go, chunks):
         d = distributed.DistContext(rank, world, unique_id=_share_id(rank, world, ids),
                                     timeout_ms=60000)
         d.set_pipeline(chunks, 16)
+        if blocks:
+            d.set_row_blocks(blocks)
         pgd = distributed.partition(g, d)
         for _ in range(2):  # twice: the staging buffers are reused
             h = pgd
             for i, lay in enumerate(layers):
-                h = lay.forward(h, _act="relu" if i == 0 else None)
+                last = i == len(layers) - 1
+                h = lay.forward(h, _act=None if last else "relu",
+                                _send_next=bool(blocks) and not last)
         d.synchronize()
         lo, hi = pgd.pg.lo, pgd.pg.hi
         ok = bool(torch.equal(h.x.view(torch.int32), want[lo:hi].view(torch.int32)))
@@ -116,10 +120,12 @@ def _layers_main(rank, world, q, ids, go, chunks):
 
 
 @needs2
-@pytest.mark.parametrize("chunks", [1, 4])
-def test_partitioned_layers_and_spmm_match_one_gpu(chunks):
+@pytest.mark.parametrize("chunks,blocks", [(1, 0), (4, 0), (1, 4), (1, 1), (2, 8)])
+def test_partitioned_layers_and_spmm_match_one_gpu(chunks, blocks):
+    """blocks > 0: each layer's output halo is sent early, row block by row
+    block, while the layer's last product runs."""
     world = min(_gpus(), 4)
-    res = _spawn(_layers_main, world, chunks)
+    res = _spawn(_layers_main, world, chunks, blocks)
     assert sum(r[3] for r in res) == 6000
     for rank, ok, ok_spmm, _, mx in res:
         assert ok, f"rank {rank}: SAGE rows differ from the single-GPU forward ({mx})"

@@ -56,6 +56,12 @@ def _rank_main(rank, world, port, n, f, ei, e, x, want, q):
         partition.exchange(plan, ext)
         need = np.concatenate([np.arange(plan.lo, plan.hi), plan.halo_ids]).astype(np.int64)
         ok_ext = np.array_equal(ext.numpy(), x[need])
+        # the early sends' order: row block by row block, same halo
+        for blocks in (1, 3, 4):
+            ext_b = torch.full((plan.n_own + plan.n_halo, f), float("nan"))
+            ext_b[: plan.n_own] = torch.from_numpy(x[plan.lo:plan.hi])
+            partition.exchange_blocks(plan, ext_b, blocks)
+            ok_ext = ok_ext and np.array_equal(ext_b.numpy(), x[need])
         res = {}
         for op in ("sum", "mean", "max"):
             got = orc.csr_aggregate(plan.row_ptr.astype(np.uint32), plan.col.astype(np.uint32),

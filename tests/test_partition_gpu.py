@@ -58,6 +58,11 @@ def test_device_plan_matches_host_plan(bg, world):
         assert np.array_equal(srow.cpu().numpy(), want.send_rows)
         lrp, lcol = _local_csr(ctx, pg)
         assert np.array_equal(lrp, want.row_ptr) and np.array_equal(lcol, want.col)
+        for blocks in (1, 3, 4, 8):
+            sf, rf = pg.row_blocks(blocks)
+            wsf, wrf = partition.row_blocks(want, blocks)
+            assert np.array_equal(sf.astype(np.int64), wsf), (rank, blocks)
+            assert np.array_equal(rf.astype(np.int64), wrf), (rank, blocks)
         pg.close()
 
 
