@@ -214,8 +214,38 @@ __device__ __forceinline__ float lds_f32(uint32_t a) {
   asm volatile("ld.shared.f32 %0, [%1];\n" : "=f"(v) : "r"(a));
   return v;
 }
+template <int OFF>
+__device__ __forceinline__ float lds_f32_off(uint32_t a) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1+%2];\n" : "=f"(v) : "r"(a), "n"(OFF));
+  return v;
+}
 __device__ __forceinline__ void cp_async16_sa(uint32_t sa, const void* g) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(sa), "l"(g) : "memory");
+}
+// the same at both addresses plus a constant byte offset
+template <int OFF>
+__device__ __forceinline__ void cp_async16_off(uint32_t sa, const void* g) {
+  asm volatile("cp.async.cg.shared.global [%0+%2], [%1+%2], 16;\n" ::"r"(sa), "l"(g), "n"(OFF)
+               : "memory");
+}
+// Source-row slices of QPT x 64 floats (16-byte copies): 16 lanes per row,
+// lane c copying chunks c, c+16, c+32, ... at constant 256-byte offsets, so
+// one index load and one address computation serve QPT copies (one copy per
+// lane per row cost 20 of an F = 256 aggregation's 106 warp instructions per
+// edge).  Rows j0, j0 + jstep, ... < cnt of the stage; da / src already
+// include the lane's first chunk.
+template <int QPT>
+__device__ __forceinline__ void copy_rows16(uint32_t da, uint32_t dstep, const float* src,
+                                            const uint32_t* sid, int j0, int jstep, int cnt,
+                                            int64_t ld_x) {
+  for (int j = j0; j < cnt; j += jstep, da += dstep) {
+    const float* g = src + (int64_t)sid[j] * ld_x;
+    cp_async16_off<0>(da, g);
+    if (QPT > 1) cp_async16_off<256>(da, g);
+    if (QPT > 2) cp_async16_off<512>(da, g);
+    if (QPT > 3) cp_async16_off<768>(da, g);
+  }
 }
 __device__ __forceinline__ void cp_async4(void* s, const void* g) {
   const unsigned sa = (unsigned)__cvta_generic_to_shared(s);
@@ -389,6 +419,10 @@ __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint
   const int ch = CP == CP_A16 ? fw >> 2 : fw;  // chunks per edge (16 or 4 bytes)
   const int cdj = tp / ch, cdq = tp - cdj * ch;
   const int cj0 = ptid / ch, cq0 = ptid - cj0 * ch;
+  // widths of 128, 192 or 256 floats: 16 lanes per row (copy_rows16; at 64
+  // floats the one-chunk-per-lane copy below is as cheap)
+  const int q16 = (CP == CP_A16 && (ch & 15) == 0 && ch >= 32) ? ch >> 4 : 0;
+  const int g_lane = ptid & 15, g_j0 = ptid >> 4, g_js = tp >> 4;
   auto issue = [&](uint32_t k) {
     if (k < nst) {
       const int slot = (int)((kg + k) % S);
@@ -396,7 +430,16 @@ __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint
       const int cnt = (int)min((uint32_t)eps, ne - k * (uint32_t)eps);  // edges in this stage
       float* sb = buf + (size_t)slot * eps * swp;
       constexpr int QB = CP == CP_A16 ? 4 : 1;  // floats per chunk
-      if (cdq == 0) {
+      if (q16) {
+        const uint32_t da = smem_u32(sb + 4 * g_lane + (size_t)g_j0 * swp);
+        const uint32_t dstep = (uint32_t)(g_js * swp) * 4u;
+        const float* src = a.x + f0 + 4 * g_lane;
+        switch (q16) {
+            case 2: copy_rows16<2>(da, dstep, src, sid, g_j0, g_js, cnt, a.ld_x); break;
+          case 3: copy_rows16<3>(da, dstep, src, sid, g_j0, g_js, cnt, a.ld_x); break;
+          default: copy_rows16<4>(da, dstep, src, sid, g_j0, g_js, cnt, a.ld_x); break;
+        }
+      } else if (cdq == 0) {
         // ch divides the pipe width: the thread's chunk q never changes
         const float* src = a.x + f0 + QB * cq0;
         float* dst = sb + QB * cq0;
@@ -475,25 +518,31 @@ __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint
     if (ONE_ROW && consumer) {
       // a single row (a giant slice): no row ends inside the stream, and the
       // add chain is the critical path, so the shared-memory reads run R
-      // edges ahead of the adds in a rolling register window
-      const float* b = buf + (size_t)slot * eps * swp + ptid;
-      const float* wb = wbuf + slot * eps;
+      // edges ahead of the adds in a rolling register window.  32-bit shared
+      // addresses throughout (generic 64-bit indexing here made the giant
+      // launch slower per edge than a giant slice inside the main launch).
+      const uint32_t swp4 = (uint32_t)swp * 4u;
+      uint32_t ra = smem_u32(buf + (size_t)slot * eps * swp + ptid);
+      const uint32_t w32 = smem_u32(wbuf + slot * eps);
       const uint32_t cnt = min((uint32_t)eps, ne - k * (uint32_t)eps);
       constexpr int R = 16;
       float v[R], wr[R];
 #pragma unroll
-      for (int u = 0; u < R; u++) {
-        v[u] = (uint32_t)u < cnt ? b[(size_t)u * swp] : 0.0f;
-        wr[u] = (HAS_W && (uint32_t)u < cnt) ? wb[u] : 0.0f;
+      for (int u = 0; u < R; u++, ra += swp4) {
+        v[u] = (uint32_t)u < cnt ? lds_f32(ra) : 0.0f;
+        wr[u] = (HAS_W && (uint32_t)u < cnt) ? lds_f32(w32 + 4u * u) : 0.0f;
       }
+      // ra: edge R's address
       uint32_t j = 0;
       for (; j + 2 * R <= cnt; j += R) {
+        const uint32_t wa = w32 + (j + R) * 4u;
 #pragma unroll
         for (int u = 0; u < R; u++) {
           const float w = (OP == OP_GCN) ? __fmul_rn(wr[u], dinv_r) : wr[u];
           acc = step<OP>(acc, v[u], w);
-          v[u] = b[(size_t)(j + R + u) * swp];
-          if (HAS_W) wr[u] = wb[j + R + u];
+          v[u] = lds_f32(ra);
+          ra += swp4;
+          if (HAS_W) wr[u] = lds_f32(wa + 4u * u);
         }
       }
 #pragma unroll
@@ -503,16 +552,16 @@ __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint
           acc = step<OP>(acc, v[u], w);
         }
       }
-      for (j += R; j < cnt; j++) {
+      for (j += R; j < cnt; j++, ra += swp4) {
         float w = 0.0f;
-        if (OP == OP_GCN) w = __fmul_rn(wb[j], dinv_r);
-        if (OP == OP_SPMM || OP == OP_SPMM_X) w = wb[j];
-        acc = step<OP>(acc, b[(size_t)j * swp], w);
+        if (OP == OP_GCN) w = __fmul_rn(lds_f32(w32 + j * 4u), dinv_r);
+        if (OP == OP_SPMM || OP == OP_SPMM_X) w = lds_f32(w32 + j * 4u);
+        acc = step<OP>(acc, lds_f32(ra), w);
       }
     } else if (consumer) {
       const uint32_t b32 = smem_u32(buf + (size_t)slot * eps * swp + ptid);
       const uint32_t swp4 = (uint32_t)swp * 4u;
-      const float* wb = wbuf + slot * eps;
+      const uint32_t w32 = smem_u32(wbuf + slot * eps);
       const uint32_t base = k * (uint32_t)eps;
       const uint32_t cnt = min((uint32_t)eps, ne - base);
       // 16-edge blocks with the lean epilogues; the generic one keeps 8 (its
@@ -526,7 +575,7 @@ __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint
 #pragma unroll
         for (int u = 0; u < UB; u++, ra += swp4) {
           v[u] = lds_f32(ra);
-          wr[u] = HAS_W ? wb[j + u] : 0.0f;
+          wr[u] = HAS_W ? lds_f32(w32 + (j + u) * 4u) : 0.0f;
         }
         if (nxt >= base + j + UB) {  // no row ends inside this block
 #pragma unroll
@@ -535,9 +584,15 @@ __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint
             acc = step<OP>(acc, v[u], w);
           }
         } else {
+          // d: edges of the block before the next row end (one compare with a
+          // constant per edge)
+          int d = (int)(nxt - (base + j));
 #pragma unroll
           for (int u = 0; u < UB; u++) {
-            while (base + j + u == nxt) finalize();
+            while (d == u) {
+              finalize();
+              d = (int)(nxt - (base + j));
+            }
             const float w = (OP == OP_GCN) ? __fmul_rn(wr[u], dinv_r) : wr[u];
             acc = step<OP>(acc, v[u], w);
           }
@@ -546,8 +601,8 @@ __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint
       for (; j < cnt; j++) {
         while (base + j == nxt) finalize();
         float w = 0.0f;
-        if (OP == OP_GCN) w = __fmul_rn(wb[j], dinv_r);
-        if (OP == OP_SPMM || OP == OP_SPMM_X) w = wb[j];
+        if (OP == OP_GCN) w = __fmul_rn(lds_f32(w32 + j * 4u), dinv_r);
+        if (OP == OP_SPMM || OP == OP_SPMM_X) w = lds_f32(w32 + j * 4u);
         acc = step<OP>(acc, lds_f32(b32 + j * swp4), w);
       }
     }
