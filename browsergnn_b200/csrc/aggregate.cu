@@ -349,6 +349,14 @@ constexpr int ST_SW = 256;    // features per slice
 constexpr int ST_GSTAGE = ST_EPS * ST_THREADS;  // floats per stage of a giant-row slice
 constexpr int ST_GSW = ST_GSTAGE / ST_THREADS;    // narrowest giant slice (ST_THREADS edges)
 
+// Source-id ring slots for an S-stage ring.  The prologue issues stages
+// 0..S-2 back to back with no barrier between them, each issue reading its
+// stage's ids and fetching (asynchronously) the ids of stage k + S - 1, so
+// the slots read (stages 0..S-2) and written (stages S-1..2S-3) there must
+// all differ: 2S - 2 slots.  Fewer (S + 1 for S = 5) let a fast thread's
+// fetch land in a slot a slower thread was still reading.
+__host__ __device__ constexpr int ids_slots(int S) { return 2 * S - 2 > S + 1 ? 2 * S - 2 : S + 1; }
+
 // shared-memory regions, large enough for both the pipe layout and the
 // giant-slice layout (ST_GSTAGE floats per stage, any slice width)
 __host__ __device__ constexpr size_t stream_data_floats(int P, int swp) {
@@ -361,14 +369,17 @@ __host__ __device__ constexpr size_t stream_w_floats(int P) {
                                                                  : (size_t)ST_S * ST_THREADS;
 }
 __host__ __device__ constexpr size_t stream_sidx_words(int P) {
-  return (size_t)P * (ST_S + 1) * ST_EPS > (size_t)(ST_S + 1) * ST_THREADS
-             ? (size_t)P * (ST_S + 1) * ST_EPS
-             : (size_t)(ST_S + 1) * ST_THREADS;
+  return (size_t)P * ids_slots(ST_S) * ST_EPS > (size_t)ids_slots(ST_S) * ST_THREADS
+             ? (size_t)P * ids_slots(ST_S) * ST_EPS
+             : (size_t)ids_slots(ST_S) * ST_THREADS;
 }
 
+// Both forms are volatile asm, like the shared-memory loads of the hot loops
+// (lds_f32): volatile asm keeps its order, so no load of a stage can be
+// scheduled above the barrier that publishes the stage.
 __device__ __forceinline__ void pipe_bar(int id, int count) {
   if (id == 0)
-    __syncthreads();
+    asm volatile("bar.sync 0;\n" ::: "memory");
   else
     asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
 }
@@ -400,15 +411,16 @@ __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint
       rinv[i] = __ddiv_rn(1.0, (double)(a.row_ptr[rb + i + 1] - a.row_ptr[rb + i]));
 
   const uint32_t nst = (ne + eps - 1) / eps;
-  // Source ids: sidx slot m % (S+1) holds stage m's ids.  Stages 0..S-2 are
+  // Source ids: sidx slot m % IDS holds stage m's ids.  Stages 0..S-2 are
   // loaded before the ring starts; issue(m) fetches stage m+S-1's ids with
   // cp.async in the same group as stage m's rows.  issue(m+S-1) runs at
   // iteration m, after the wait that completes stage m's group and the
   // barrier that publishes it, so no copy ever waits on an index load.
+  constexpr int IDS = ids_slots(S);
   auto fetch_ids = [&](uint32_t m) {
     const uint32_t e = m * (uint32_t)eps + (uint32_t)ptid;
     if (ptid < eps && m < nst && e < ne)
-      cp_async4(sidx + (m % (S + 1)) * eps + ptid, a.src_of + e0 + e);
+      cp_async4(sidx + (m % IDS) * eps + ptid, a.src_of + e0 + e);
   };
   // Row slices move as cp.async copies of 16 (CP_A16) or 4 bytes spread over
   // the pipe, consecutive threads on consecutive chunks of one row; per-edge
@@ -416,21 +428,28 @@ __device__ __forceinline__ void stream_range(const AggArgs& a, uint32_t rb, uint
   // Copy c of a stage (c = ptid, ptid + tp, ...) is chunk q = c % ch of
   // edge j = c / ch; the thread walks (j, q) incrementally (ch <= tp always),
   // so the copy loop has no integer division.
+  // ONE_ROW (a giant slice, fw <= 128): the consumer warps only reduce and
+  // the other warps copy (consumer warps that also issued copies ran the
+  // chain at about 6 ns per edge, 5 without)
+  const int cons = ONE_ROW ? ((fw + 31) & ~31) : 0;
+  const int ctp = tp - cons, cpt = ptid - cons;  // copying threads, this one's rank
   const int ch = CP == CP_A16 ? fw >> 2 : fw;  // chunks per edge (16 or 4 bytes)
-  const int cdj = tp / ch, cdq = tp - cdj * ch;
-  const int cj0 = ptid / ch, cq0 = ptid - cj0 * ch;
+  const int cdj = ctp / ch, cdq = ctp - cdj * ch;
+  const int cj0 = cpt / ch, cq0 = cpt - cj0 * ch;
   // widths of 128, 192 or 256 floats: 16 lanes per row (copy_rows16; at 64
   // floats the one-chunk-per-lane copy below is as cheap)
   const int q16 = (CP == CP_A16 && (ch & 15) == 0 && ch >= 32) ? ch >> 4 : 0;
-  const int g_lane = ptid & 15, g_j0 = ptid >> 4, g_js = tp >> 4;
+  const int g_lane = cpt & 15, g_j0 = cpt >> 4, g_js = ctp >> 4;
   auto issue = [&](uint32_t k) {
     if (k < nst) {
       const int slot = (int)((kg + k) % S);
-      const uint32_t* sid = sidx + (k % (S + 1)) * eps;
+      const uint32_t* sid = sidx + (k % IDS) * eps;
       const int cnt = (int)min((uint32_t)eps, ne - k * (uint32_t)eps);  // edges in this stage
       float* sb = buf + (size_t)slot * eps * swp;
       constexpr int QB = CP == CP_A16 ? 4 : 1;  // floats per chunk
-      if (q16) {
+      if (cpt < 0) {
+        // a consumer warp of a giant slice: no row copies
+      } else if (q16) {
         const uint32_t da = smem_u32(sb + 4 * g_lane + (size_t)g_j0 * swp);
         const uint32_t dstep = (uint32_t)(g_js * swp) * 4u;
         const float* src = a.x + f0 + 4 * g_lane;
@@ -683,7 +702,7 @@ __global__ void __launch_bounds__(ST_THREADS, 2)
   const int bar_id = P == 1 ? 0 : pipe + 1;
   float* pdata = data + (size_t)pipe * ST_S * ST_EPS * swp;
   float* pwb = wb + pipe * ST_S * ST_EPS;
-  uint32_t* psidx = sidx + pipe * (ST_S + 1) * ST_EPS;
+  uint32_t* psidx = sidx + pipe * ids_slots(ST_S) * ST_EPS;
   uint32_t* prps = rps + pipe * (ST_RMAX + 1);
   float* prdv = rdv + pipe * ST_RMAX;
   double* prinv = rinv ? rinv + pipe * ST_RMAX : nullptr;
@@ -705,7 +724,7 @@ __global__ void __launch_bounds__(ST_THREADS, 2)
 // ring than the shared-SM pipes since the whole SM's shared memory is its.
 constexpr int GS_S = 5;  // ring stages of a giant-slice CTA
 constexpr size_t giant_smem_bytes() {
-  return ((size_t)GS_S * ST_GSTAGE + (size_t)GS_S * ST_THREADS + (size_t)(GS_S + 1) * ST_THREADS +
+  return ((size_t)GS_S * ST_GSTAGE + (size_t)GS_S * ST_THREADS + (size_t)ids_slots(GS_S) * ST_THREADS +
           16) * 4;
 }
 
@@ -716,7 +735,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
   float* data = reinterpret_cast<float*>(gt_smem4);
   float* wb = data + (size_t)GS_S * ST_GSTAGE;
   uint32_t* sidx = reinterpret_cast<uint32_t*>(wb + GS_S * ST_THREADS);
-  uint32_t* rps = sidx + (GS_S + 1) * ST_THREADS;  // one row per item: 2 offsets
+  uint32_t* rps = sidx + ids_slots(GS_S) * ST_THREADS;  // one row per item: 2 offsets
   float* rdv = reinterpret_cast<float*>(rps + 4);
   const int F = a.num_features;
   const uint32_t gs = (uint32_t)((F + gsw - 1) / gsw);

@@ -82,3 +82,32 @@ def test_giant_rows_spmm_bit_exact(bg, f):
     cv = csr.values.cpu().numpy()
     want = orc.spmm_rows(rp, ci, cv, x, f).reshape(n, f)
     assert_bits_equal(out, want, f"SpMM F={f}")
+
+
+def test_giant_row_reads_each_source_once(bg):
+    """A 150,000-edge hub row summed over indicator features (feature c of
+    node i is 1 when i mod 32 == c): every column must count exactly the hub's
+    sources congruent to c.  A source-id slot overwritten before its stage was
+    copied shows up here as a row counted in the wrong column."""
+    import torch
+
+    from browsergnn_b200.backend import ptr
+
+    n, f, deg = 40000, 32, 150000
+    rng = np.random.default_rng(11)
+    src = rng.integers(0, n, deg).astype(np.uint32)
+    bs = rng.integers(0, n, 200000).astype(np.uint32)
+    bd = rng.integers(1, n, 200000).astype(np.uint32)
+    ei = np.concatenate([src, bs, np.zeros(deg, np.uint32), bd])
+    g = bg.GraphData(x=np.zeros((n, 1), np.float32), numNodes=n, numFeatures=1, edgeIndex=ei,
+                     numEdges=deg + 200000)
+    dg = g.device_graph()
+    idx = torch.arange(n, device="cuda")
+    xm = torch.zeros((n, f), device="cuda")
+    xm[idx, idx % f] = 1.0
+    out = torch.empty((n, f), device="cuda")
+    for _ in range(3):
+        dg.ctx.call("bgnn_aggregate", dg.h, 0, ptr(xm), f, ptr(out))
+        got = out[0].cpu().numpy()
+        want = np.bincount(src % f, minlength=f).astype(np.float32)
+        assert np.array_equal(got, want), (got - want)
