@@ -54,6 +54,7 @@ SIGNATURES = {
     "bgnn_ctx_create": [_I, ctypes.POINTER(_P)],
     "bgnn_ctx_destroy": [_P],
     "bgnn_ctx_set_stream": [_P, _P],
+    "bgnn_ctx_set_sm_budget": [_P, _U32],
     "bgnn_ctx_set_math": [_P, _I],
     "bgnn_ctx_synchronize": [_P],
     "bgnn_last_error": [_P],

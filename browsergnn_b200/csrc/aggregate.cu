@@ -722,7 +722,7 @@ __global__ void __launch_bounds__(ST_THREADS, 2)
 // Giant-row slices in their own launch: one CTA per slice, alone on its SM
 // (its shared memory request leaves no room for a second CTA), with a deeper
 // ring than the shared-SM pipes since the whole SM's shared memory is its.
-constexpr int GS_S = 5;  // ring stages of a giant-slice CTA
+constexpr int GS_S = 6;  // ring stages of a giant-slice CTA (208 KB of shared memory)
 constexpr size_t giant_smem_bytes() {
   return ((size_t)GS_S * ST_GSTAGE + (size_t)GS_S * ST_THREADS + (size_t)ids_slots(GS_S) * ST_THREADS +
           16) * 4;

@@ -143,6 +143,12 @@ extern "C" int bgnn_ctx_set_stream(bgnn_ctx* ctx, void* s) {
   return BGNN_OK;
 }
 
+extern "C" int bgnn_ctx_set_sm_budget(bgnn_ctx* ctx, uint32_t sms) {
+  if (!ctx) return BGNN_ERR_INVALID_ARG;
+  ctx->grid_sms = sms >= (uint32_t)ctx->num_sms ? 0 : (int)sms;
+  return BGNN_OK;
+}
+
 extern "C" int bgnn_ctx_set_math(bgnn_ctx* ctx, int mode) {
   if (!ctx) return BGNN_ERR_INVALID_ARG;
   if (mode != BGNN_MATH_FAST && mode != BGNN_MATH_EXACT && mode != BGNN_MATH_TENSOR)

@@ -111,6 +111,11 @@ BGNN_API int bgnn_ctx_destroy(bgnn_ctx* ctx);
  * stream).  A new context starts on a non-blocking stream of its own. */
 BGNN_API int bgnn_ctx_set_stream(bgnn_ctx* ctx, void* cuda_stream);
 BGNN_API int bgnn_ctx_set_math(bgnn_ctx* ctx, int math_mode);
+/* Persistent launches (the streaming aggregation, the tensor-core X*W) size
+ * their grids for at most `sms` SMs, leaving the others to work the caller
+ * runs beside them on another stream (0 or >= the GPU's SMs: all).  No
+ * counterpart in the reference, which runs one kernel at a time. */
+BGNN_API int bgnn_ctx_set_sm_budget(bgnn_ctx* ctx, uint32_t sms);
 /* Waits for the context's stream and reports any kernel-raised error. */
 BGNN_API int bgnn_ctx_synchronize(bgnn_ctx* ctx);
 BGNN_API const char* bgnn_last_error(const bgnn_ctx* ctx);

@@ -121,6 +121,28 @@ def test_coo_to_csr_bit_exact(bg, torch, nnz, m, ncol):
     assert np.array_equal(rp, orp) and np.array_equal(ci, oci)
 
 
+def test_sm_budget_same_bits(bg, torch):
+    """An aggregation held to a few SMs (bgnn_ctx_set_sm_budget) gives the
+    same bits as one on the whole GPU: only the grid shrinks."""
+    from browsergnn_b200.backend import ptr
+
+    n, f = 20000, 64
+    ei, e = rand_graph(n, 300000, seed=4, hub_deg=60000, loops=3, dup=30)
+    g = bg.GraphData(x=np.zeros((n, 1), np.float32), numNodes=n, numFeatures=1, edgeIndex=ei,
+                     numEdges=e)
+    dg = g.device_graph()
+    x = torch.randn((n, f), device="cuda", generator=torch.Generator("cuda").manual_seed(2))
+    full = torch.empty((n, f), device="cuda")
+    few = torch.empty((n, f), device="cuda")
+    dg.ctx.call("bgnn_aggregate", dg.h, 1, ptr(x), f, ptr(full))
+    try:
+        dg.ctx.call("bgnn_ctx_set_sm_budget", 12)
+        dg.ctx.call("bgnn_aggregate", dg.h, 1, ptr(x), f, ptr(few))
+    finally:
+        dg.ctx.call("bgnn_ctx_set_sm_budget", 0)
+    assert torch.equal(full.view(torch.int32), few.view(torch.int32))
+
+
 def test_coo_to_csr_without_values(bg, torch):
     """bgnn_coo_to_csr_dev with no input values (all ones, fromEdgeIndex) and
     with no value output: the same rows and columns as the oracle."""
