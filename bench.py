@@ -1099,9 +1099,10 @@ def main():
     ap.add_argument("--chunks", type=int, default=None,
                     help="N>1: column chunks of the halo exchange, each aggregated as it lands "
                          "(default 1)")
-    ap.add_argument("--row-blocks", type=int, default=4,
+    ap.add_argument("--row-blocks", type=int, default=-1,
                     help="N>1: row blocks of each layer's last product whose rows are sent to "
-                         "the peers as they are written (0: no early sends)")
+                         "the peers as they are written (0: no early sends; default: 4 from 4 "
+                         "GPUs up, where the exchange outlasts x*W_self, else none)")
     ap.add_argument("--reserve-sms", type=int, default=16,
                     help="N>1: SMs the aggregation leaves to NCCL while chunks are in flight")
     ap.add_argument("--profile", choices=["small", "full-agg", "csr", "csr-small", "linear", "gat",
@@ -1162,6 +1163,11 @@ def main():
         dctx = distributed.DistContext(rank, world, device=local, timeout_ms=120_000)
         if args.chunks is not None:
             dctx.set_pipeline(args.chunks, args.reserve_sms)
+        if args.row_blocks < 0:
+            # at 2 GPUs x*W_self (3.4 ms at F=256) hides the 1.2 ms exchange and
+            # early sends only add contention (25.6 vs 24.9 ms per step); at 8
+            # the exchange (1.35 ms) outlasts it (0.9 / 0.3 ms)
+            args.row_blocks = 4 if world >= 4 else 0
         if args.row_blocks:
             dctx.set_row_blocks(args.row_blocks)
         torch.cuda.synchronize()
